@@ -1,0 +1,178 @@
+/*
+ * hexgen2_b200 — C ABI of the B200 (sm_100a) kernels behind the HexGen-2 prefill/decode path.
+ *
+ * Conventions shared by every entry point:
+ *   - pointers are device pointers unless the name says "host";
+ *   - sizes and strides are int64 element counts unless the name says "bytes";
+ *   - `dtype` is an hx_dtype; `stream` is a cudaStream_t passed as void*;
+ *   - the return value is an hx_status; on failure hx_last_error() describes it;
+ *   - no entry point allocates device memory unless its comment says so: scratch space is
+ *     passed in by the caller (size from the matching *_workspace() query).
+ *
+ * Reference interfaces replaced (paths are inside the HexGen-2 project):
+ *   hexgen/hexgen_core/modules/rms_norm.py:13-15, modules/block.py:125-158 and
+ *   models/gpt.py:388-397 (residual add + TorchRMSNorm), modules/embedding.py:37-51 and
+ *   :111-124 (token embedding), modules/mha.py:255-288 and flash_attn RotaryEmbedding used at
+ *   mha.py:557 (rotary + KV-cache write), nn.Linear at mha.py:395/:412, mlp.py:73-87 and
+ *   models/gpt.py:440/:476 (projections), flash_attn_kvpacked_func at mha.py:141 (prefill and
+ *   decode attention), hexgen2/model.py:81 and :103-109 (live KV slice / re-expansion),
+ *   hexgen2/transport.py:44-80 (packet transfer of the KV cache), hexgen2/model.py:82/:117
+ *   (greedy argmax).
+ */
+#ifndef HEXGEN2_B200_H
+#define HEXGEN2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum hx_dtype { HX_F32 = 0, HX_F16 = 1, HX_BF16 = 2 } hx_dtype;
+
+typedef enum hx_status {
+  HX_OK = 0,
+  HX_ERR_INVALID = 1,     /* bad argument (shape, stride, alignment, null pointer) */
+  HX_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  HX_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  HX_ERR_DEVICE = 4       /* a kernel reported a device-side error (see hx_device_error) */
+} hx_status;
+
+typedef enum hx_epilogue {
+  HX_EPI_NONE = 0,     /* C = round(A B^T) */
+  HX_EPI_RESIDUAL = 1, /* C = round(round(A B^T) + R)   (out_proj / fc2 + residual add) */
+  HX_EPI_SWIGLU = 2    /* B rows interleaved [up16|gate16]...; C[:, j] = up_j * silu(gate_j) */
+} hx_epilogue;
+
+/* ---------------------------------------------------------------- library / errors */
+int hx_abi_version(void);
+const char* hx_last_error(void);
+/* Reads (and, if clear != 0, resets) the device-side error word that kernels set when a
+ * bounded wait gives up. Synchronises the current device. */
+int hx_device_error(int clear);
+int hx_sm_count(void);
+
+/* ---------------------------------------------------------------- embedding + norms */
+/* out[r, :] = table[ids[r] - vocab_start, :] when vocab_start <= ids[r] < vocab_start+vocab_rows,
+ * else zeros (vocab-parallel shard). Replaces GPT2Embeddings / VocabParallelEmbedding forward
+ * (hexgen/hexgen_core/modules/embedding.py:37-51, :111-124). */
+int hx_embedding(const int64_t* ids, int64_t rows, const void* table, int64_t vocab_start,
+                 int64_t vocab_rows, int64_t hidden, void* out, int dtype, void* stream);
+
+/* Fused embedding lookup + first-block RMSNorm (TP = 1):
+ * residual_out[r] = table[ids[r]]; normed_out[r] = RMSNorm(residual_out[r]) * weight.
+ * Replaces embedding.py:37-51 followed by block.py:126-129 for layer 0. */
+int hx_embed_rmsnorm(const int64_t* ids, int64_t rows, const void* table, int64_t hidden,
+                     const void* weight, float eps, void* residual_out, void* normed_out,
+                     int dtype, void* stream);
+
+/* Residual add + RMSNorm with the reference's rounding points:
+ *   res = add ? round(x + add) : x;  residual_out (if non-null) = res;
+ *   out = round(round(res * rsqrt(mean(res^2) + eps)) * weight)   (f32 statistics)
+ * Row r of x/add is read at r*in_stride, outputs written at r*out_stride.
+ * Replaces block.py:126-129 / :155-158 + rms_norm.py:13-15, and gpt.py:388-397 (ln_f). */
+int hx_rmsnorm(const void* x, const void* add, void* residual_out, void* out,
+               const void* weight, int64_t rows, int64_t hidden, int64_t in_stride,
+               int64_t out_stride, float eps, int dtype, void* stream);
+
+/* ---------------------------------------------------------------- rotary + cache write */
+/* qkv: [batch, seqlen, (n_heads + 2*n_heads_kv) * head_dim] packed Wqkv output.
+ * For token s of sequence b at position p = pos_start[b] + s (pos_start: device int32[batch]):
+ *   q_out[b, s, h, :]              = rope(q[b, s, h, :], p)
+ *   cache[cache_batch_offset + b, p, 0, hk, :] = rope(k[b, s, hk, :], p)
+ *   cache[cache_batch_offset + b, p, 1, hk, :] = v[b, s, hk, :]
+ * cos/sin tables are [table_rows, head_dim/2] in `dtype` (the reference caches them in the
+ * activation dtype). interleaved != 0 rotates pairs (x[2i], x[2i+1]) (GPT-J style, what the
+ * native Llama model uses); 0 rotates halves (GPT-NeoX style).
+ * Replaces flash_attn RotaryEmbedding (mha.py:382-384, :557) + _update_kv_cache copy
+ * (mha.py:255-288). */
+int hx_rotary_cache_write(const void* qkv, int64_t batch, int64_t seqlen, int64_t n_heads,
+                          int64_t n_heads_kv, int64_t head_dim, const int32_t* pos_start,
+                          const void* cos_table, const void* sin_table, int64_t table_rows,
+                          int interleaved, void* q_out, void* cache, int64_t cache_batch_stride,
+                          int64_t cache_seq_stride, int64_t cache_batch_offset,
+                          int64_t cache_max_seq, int dtype, void* stream);
+
+/* ---------------------------------------------------------------- projections */
+/* C[m, n] = A[m, k] * B[n, k]^T (both operands K-contiguous, nn.Linear weight layout), f32
+ * accumulation, with the epilogue `epilogue` (hx_epilogue). f16/bf16 run on tcgen05 tensor
+ * cores fed by TMA; f32 runs on a CUDA-core kernel (exact f32 products).
+ * Alignment (f16/bf16): A, B 16-byte aligned; lda, ldb multiples of 8.
+ * For HX_EPI_SWIGLU, n counts interleaved B rows (2 * intermediate) and C has n/2 columns.
+ * `workspace` may be NULL when hx_gemm_workspace() returns 0 for the shape; otherwise it must
+ * hold that many bytes (split-K partial sums).
+ * Replaces nn.Linear (mha.py:395/:412, mlp.py:73-87, gpt.py:440) + the residual add of
+ * block.py:155-158 + the SwiGLU of mlp.py:79-87. */
+int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
+            int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
+            int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
+            void* stream);
+size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
+
+/* ---------------------------------------------------------------- attention */
+/* Causal prefill attention over the KV cache written by hx_rotary_cache_write.
+ * q: [batch, seqlen_q, n_heads, head_dim]; keys/values are cache[cache_batch_offset + b,
+ * 0 : pos_start[b] + seqlen_q]; query s of sequence b (position pos_start[b] + s) attends to
+ * key positions <= pos_start[b] + s. out: [batch, seqlen_q, n_heads, head_dim].
+ * Replaces flash_attn_kvpacked_func(..., causal=True) at mha.py:141/:569. */
+int hx_prefill_attention(const void* q, const void* cache, int64_t cache_batch_stride,
+                         int64_t cache_seq_stride, int64_t cache_batch_offset,
+                         const int32_t* pos_start, int64_t batch, int64_t seqlen_q,
+                         int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
+                         float softmax_scale, void* out, int dtype, void* stream);
+
+/* Single-query decode attention, split over the key axis (flash-decoding), GQA aware.
+ * q: [batch, n_heads, head_dim]; sequence b attends to cache[b, 0 : seqlens_k[b]]
+ * (seqlens_k: device int32[batch], each <= max_seqlen_k). out: [batch, n_heads, head_dim].
+ * workspace: hx_decode_attention_workspace() bytes of split partials.
+ * Replaces flash_attn_kvpacked_func(..., causal=False) with q_len 1 at mha.py:565-569. */
+int hx_decode_attention(const void* q, const void* cache, int64_t cache_batch_stride,
+                        int64_t cache_seq_stride, const int32_t* seqlens_k, int64_t batch,
+                        int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
+                        int64_t max_seqlen_k, float softmax_scale, void* out, void* workspace,
+                        size_t workspace_bytes, int dtype, void* stream);
+size_t hx_decode_attention_workspace(int64_t batch, int64_t n_heads, int64_t head_dim,
+                                     int64_t max_seqlen_k);
+
+/* ---------------------------------------------------------------- sampling */
+/* out_idx[r] = first index of the maximum of logits[r, 0:cols] (torch.argmax semantics).
+ * Replaces logits.argmax(-1) at hexgen2/model.py:82 and :117. */
+int hx_argmax(const void* logits, int64_t rows, int64_t cols, int64_t ld, int64_t* out_idx,
+              int dtype, void* stream);
+
+/* ---------------------------------------------------------------- KV handoff */
+/* Gather-pack of live cache rows for n_req requests into one contiguous buffer.
+ * Request r's source is viewed as [n_outer][cap_rows][row_bytes] starting at src_ptrs[r]
+ * (outer stride outer_stride_bytes, row stride row_stride_bytes); its first live_rows[r]
+ * rows of every outer slice are written densely to dst + dst_offsets[r] as
+ * [n_outer][live_rows[r]][row_bytes]. src_ptrs/live_rows/dst_offsets are device arrays.
+ * dst may be a peer GPU's buffer (peer access or IPC mapping): the copy then crosses NVLink
+ * inside the kernel. Bytes are copied verbatim (row_bytes and all offsets multiples of 16).
+ * Replaces the live slice t[:, :L].contiguous() at hexgen2/model.py:81 and the per-layer
+ * sends of hexgen2/transport.py:54-59. */
+int hx_kv_pack(const uint64_t* src_ptrs, const int64_t* live_rows, const int64_t* dst_offsets,
+               int64_t n_req, int64_t n_outer, int64_t outer_stride_bytes,
+               int64_t row_stride_bytes, int64_t row_bytes, int64_t max_live_rows, void* dst,
+               void* stream);
+/* Inverse of hx_kv_pack: scatter packed rows back into capacity-sized caches (dst_ptrs[r]).
+ * Replaces the re-expansion into a full cache at hexgen2/model.py:103-109. */
+int hx_kv_unpack(const void* src, const int64_t* src_offsets, const int64_t* live_rows,
+                 const uint64_t* dst_ptrs, int64_t n_req, int64_t n_outer,
+                 int64_t outer_stride_bytes, int64_t row_stride_bytes, int64_t row_bytes,
+                 int64_t max_live_rows, void* stream);
+
+/* Peer access / IPC plumbing for the NVLink handoff (one process per GPU). */
+int hx_enable_peer_access(int peer_device);
+int hx_ipc_get_handle(const void* device_ptr, void* handle_out_64_bytes);
+int hx_ipc_open_handle(const void* handle_64_bytes, void** device_ptr_out);
+int hx_ipc_close_handle(void* device_ptr);
+/* Copy-engine peer copy (cudaMemcpyPeerAsync) of `bytes` on `stream`. */
+int hx_peer_copy(void* dst, int dst_device, const void* src, int src_device, size_t bytes,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HEXGEN2_B200_H */
