@@ -1,0 +1,348 @@
+"""Benchmark: HexGen-2 prefill/decode hot path on B200 (driver contract: one JSON line).
+
+Workload (the one the headline metric names): Llama-2-7B architecture
+(32 layers, hidden 4096, 32 heads MHA, head_dim 128, intermediate 11008, vocab 32000),
+random-init bf16 weights N(0, 0.02); a batch of B requests (default 32) with prompt lengths
+drawn lognormal(mean 1024, sigma 0.5) clipped to [128, 4096] (mu = ln 1024 - sigma^2/2), token
+ids uniform; greedy decode to 256 output tokens. One step = prefill every request (TTFT per
+request) + decode the batch (ragged per-sequence lengths) to 256 tokens.
+  N = 1: colocated on one GPU (prefill writes straight into the decode cache slots).
+  N > 1: prefill group = ranks [0, N/2), decode group = ranks [N/2, N), tensor-parallel
+         (TP = N/2) inside each group over NCCL; each prefill rank hands its KV shard to decode
+         rank r + N/2 over NVLink (IPC-mapped buffer written by the gather-pack kernel).
+
+value   = decode tokens/s (tokens produced by decode steps / decode-phase device time), summed
+          over the whole job; ttft_p50_ms alongside.
+e2e     = the same batch through the public API (Engine.serve_batch) from pinned host token
+          ids to host token lists, H2D/D2H inside the timed region: generated tokens/s.
+--impl reference: the reference algorithm on the host CPU (the oracle port), bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+LLAMA2_7B = dict(vocab_size=32000, hidden_size=4096, intermediate_size=11008,
+                 num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=32,
+                 rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=4096 + 512)
+METRIC = "decode tokens/s + p50 TTFT (Llama-2-7B arch, bf16)"
+
+
+def prompt_lengths(batch: int, seed: int) -> list[int]:
+    g = torch.Generator().manual_seed(seed)
+    sigma = 0.5
+    mu = math.log(1024) - sigma * sigma / 2
+    z = torch.randn(batch, generator=g, dtype=torch.float64)
+    return [int(min(4096, max(128, round(math.exp(mu + sigma * float(v)))))) for v in z]
+
+
+def make_prompts(batch: int, seed: int, vocab: int) -> list[list[int]]:
+    lens = prompt_lengths(batch, seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    return [torch.randint(0, vocab, (L,), generator=g).tolist() for L in lens]
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (median SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------------------------
+# Native arm, N = 1 (colocated)
+# ------------------------------------------------------------------------------------------
+def kernel_work(name_times: dict, cfg: dict, lens: list[int], out_len: int, steps: int) -> dict:
+    """Algorithmic bytes / flops per kernel class for the timed steps (for the roofline)."""
+    h, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"]
+    hq, hk = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    d = h // hq
+    B = len(lens)
+    # Decode attention: every decode step reads the live K and V of every sequence per layer.
+    dec_bytes = 0
+    for s in range(out_len - 1):
+        for Lb in lens:
+            dec_bytes += 2 * hk * d * (Lb + s + 1) * 2 + 2 * hq * d * 2
+    dec_bytes *= L * steps
+    return {"decode_attention": {"bytes": dec_bytes}}
+
+
+def run_native_single(args) -> dict:
+    import hexgen2_b200 as hx
+    from hexgen2_b200 import ops
+    from hexgen2_b200.gpt import CacheState
+
+    torch.cuda.set_device(0)
+    cfg = dict(LLAMA2_7B)
+    eng = hx.Engine.from_config(cfg, dtype="bfloat16", seed=args.seed)
+    model = eng.model
+    B, out_len = args.batch, args.out_len
+    prompts = make_prompts(B, args.seed, cfg["vocab_size"])
+    lens = [len(p) for p in prompts]
+    capacity = max(lens) + out_len
+    cache = model.allocate_inference_cache(B, capacity)
+    ids_dev = [torch.tensor([p], dtype=torch.long, device="cuda") for p in prompts]
+    first = torch.empty(B, dtype=torch.long, device="cuda")
+    lengths = torch.empty(B, dtype=torch.int32, device="cuda")
+    lens_dev = torch.tensor(lens, dtype=torch.int32, device="cuda")
+
+    def one_step(ttft_events):
+        for b in range(B):
+            st = CacheState(capacity, max_batch_size=B, batch_size_offset=b,
+                            key_value_memory_dict=cache)
+            logits = model(ids_dev[b], inference_params=st, last_token_only=True).logits
+            ops.argmax(logits, out=first[b:b + 1])
+            if ttft_events is not None:
+                ttft_events[b].record()
+        lengths.copy_(lens_dev)
+        dec0 = torch.cuda.Event(enable_timing=True)
+        dec1 = torch.cuda.Event(enable_timing=True)
+        dec0.record()
+        toks = eng.decode_batch(first, cache, lengths, out_len - 1)
+        dec1.record()
+        return toks, dec0, dec1
+
+    for _ in range(args.warmup):
+        one_step(None)
+    torch.cuda.synchronize()
+
+    ops.LAUNCHES = 0
+    ops.PROFILE = [] if args.profile_kernels else None
+    step_marks, ttfts, decs = [], [], []
+    with ClockSampler(0) as clocks:
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            s0 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(B)]
+            toks, d0, d1 = one_step(ev)
+            step_marks.append(s0)
+            ttfts.append(ev)
+            decs.append((d0, d1))
+        t1.record()
+        torch.cuda.synchronize()
+    launches = ops.LAUNCHES
+    prof = ops.PROFILE
+    ops.PROFILE = None
+    total_ms = t0.elapsed_time(t1)
+    dec_ms = sum(a.elapsed_time(b) for a, b in decs)
+    ttft_ms = [s.elapsed_time(e) for s, evs in zip(step_marks, ttfts) for e in evs]
+    dec_tokens = B * (out_len - 1) * args.steps
+    value = dec_tokens / (dec_ms / 1e3)
+
+    # Per-kernel device time over the timed region.
+    per_kernel = {}
+    if prof:
+        for name, a, b in prof:
+            t = a.elapsed_time(b)
+            k = per_kernel.setdefault(name, [0.0, 0])
+            k[0] += t
+            k[1] += 1
+    work = kernel_work(per_kernel, cfg, lens, out_len, args.steps)
+    pk = peaks()
+    roofline = None
+    if "decode_attention" in per_kernel:
+        ms, n = per_kernel["decode_attention"]
+        achieved = work["decode_attention"]["bytes"] / (ms / 1e3) / 1e9
+        roofline = {"kernel": "decode_attention", "bound": "hbm", "achieved": round(achieved, 1),
+                    "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                    "traffic": None, "peak_source": pk["source"],
+                    "launches": n, "avg_launch_us": round(ms * 1e3 / n, 2)}
+
+    # End to end through the public API: pinned host prompts in, host token lists out.
+    e2e = run_e2e(eng, prompts, out_len, args)
+
+    # Serial reference-algorithm baseline on the host cores (bounded sample).
+    cpu = cpu_baseline(args) if args.cpu_baseline else None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, uniform token ids, lognormal prompt lengths)",
+        "ttft_p50_ms": round(statistics.median(ttft_ms), 2),
+        "config": {"workload": "Llama-2-7B arch colocated on 1 GPU (BASELINE config 3, 1-GPU sweep)",
+                   "model": "llama-2-7b-arch", "batch": B, "prompt_lens_mean": round(sum(lens) / B, 1),
+                   "prompt_lens_minmax": [min(lens), max(lens)], "output_len": out_len,
+                   "parallelism": "colocated prefill+decode, TP1",
+                   "l2": "inputs larger than L2 (13.5 GB weights + KV caches stream every step)"},
+        "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
+        "clocks": clocks.summary(), "cpu_baseline": cpu,
+        "kernel_ms": {k: round(v[0], 2) for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])},
+    }
+    return line
+
+
+def run_e2e(eng, prompts, out_len, args) -> dict:
+    B = len(prompts)
+    flat = [t for p in prompts for t in p]
+    host = torch.tensor(flat, dtype=torch.long).pin_memory()
+    for _ in range(1):
+        eng.serve_batch(host, [len(p) for p in prompts], out_len)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.e2e_steps):
+        out = eng.serve_batch(host, [len(p) for p in prompts], out_len)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    assert len(out) == B and all(len(o) == out_len for o in out)
+    return {"value": round(B * out_len * args.e2e_steps / (ms / 1e3), 2), "unit": "tokens/s",
+            "what": "generated tokens/s through Engine.serve_batch (prefill + decode, host in/out)",
+            "h2d_bytes_per_step": host.numel() * 8, "d2h_bytes_per_step": B * out_len * 8,
+            "steps": args.e2e_steps}
+
+
+# ------------------------------------------------------------------------------------------
+# Reference algorithm on the CPU (the oracle port): bounded sample, extrapolated per layer.
+# ------------------------------------------------------------------------------------------
+def cpu_baseline(args, threads=None) -> dict:
+    from oracle.llama_ref import LlamaShape, OracleModel, random_native_state
+
+    if threads:
+        torch.set_num_threads(threads)
+    cores = torch.get_num_threads()
+    cfg = LLAMA2_7B
+    shape = LlamaShape.from_hf(cfg)
+    shape.num_layers = 1
+    state = random_native_state(shape, seed=args.seed, dtype=torch.bfloat16)
+    model = OracleModel(shape, state, torch.bfloat16, attention="torch")
+    prompts = make_prompts(args.batch, args.seed, cfg["vocab_size"])
+    prompt = prompts[0][:512]
+    steps = 3
+    t0 = time.perf_counter()
+    first, cache, _ = model.prefill(prompt, steps + 1)
+    t1 = time.perf_counter()
+    model.decode(first, cache, len(prompt), steps + 1)
+    t2 = time.perf_counter()
+    # One layer measured; the 7B model has 32 (embedding and LM head are small next to them,
+    # their share is added from one extra LM-head timing).
+    lm = torch.randn(1, cfg["hidden_size"]).bfloat16()
+    w = state["lm_head.weight"]
+    t3 = time.perf_counter()
+    for _ in range(3):
+        torch.nn.functional.linear(lm, w)
+    lm_s = (time.perf_counter() - t3) / 3
+    layer_decode_s = (t2 - t1) / steps - lm_s
+    per_token_s = cfg["num_hidden_layers"] * layer_decode_s + lm_s
+    prefill_s = cfg["num_hidden_layers"] * ((t1 - t0) - lm_s) + lm_s
+    return {"value": round(1.0 / per_token_s, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": (f"oracle (reference algorithm, torch CPU bf16) on 1 of 32 Llama-2-7B layers: "
+                       f"prefill {len(prompt)} tokens + {steps} decode steps at batch 1, extrapolated "
+                       f"to 32 layers + LM head"),
+            "prefill_ms_extrapolated": round(prefill_s * 1e3, 1)}
+
+
+def run_reference(args) -> dict:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    cpu = cpu_baseline(args, threads=threads)
+    return {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "Llama-2-7B arch (BASELINE config 3), CPU sample",
+                       "model": "llama-2-7b-arch", "batch": 1},
+            "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--out-len", type=int, default=256)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-profile", dest="profile_kernels", action="store_false")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        line = run_reference(args)
+    elif args.gpus == 1:
+        line = run_native_single(args)
+    else:
+        from hexgen2_b200.disagg import run_bench_disaggregated
+        line = run_bench_disaggregated(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,4 +1,5 @@
-// K4: causal prefill attention over the KV cache (CUDA-core version).
+// K4: causal prefill attention over the KV cache (CUDA-core kernel: f32 and head_dim 32;
+// f16/bf16 with head_dim 64/128 run on the tcgen05 kernel in attn_prefill_tc.cu).
 //
 // Semantics: flash_attn_kvpacked_func(q, kv, causal=True) as called by the native model
 // during prefill (hexgen/hexgen_core/modules/mha.py:566-569), with FlashAttention-2's
@@ -27,7 +28,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
     const T* __restrict__ q, const T* __restrict__ cache, int64_t cbs, int64_t css,
     int64_t cache_batch_offset, const int32_t* __restrict__ pos_start, int seqlen_q,
-    int n_heads, int n_heads_kv, float scale_log2, T* __restrict__ out) {
+    int n_heads, int n_heads_kv, int causal, float scale_log2, T* __restrict__ out) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   PSmem<D>& sm = *reinterpret_cast<PSmem<D>*>(smem_raw);
   const int qblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -52,7 +53,9 @@ __global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) o[i][j] = 0.f;
   }
-  const int key_end = p0 + q0 + nq;  // exclusive: last query sees keys <= p0 + q0 + nq - 1
+  // Exclusive key bound: with causal masking the last query of the block sees keys
+  // <= p0 + q0 + nq - 1; without it every query sees all p0 + seqlen_q keys.
+  const int key_end = causal ? p0 + q0 + nq : p0 + seqlen_q;
   const T* kb = cache + (cache_batch_offset + b) * cbs + (int64_t)hk * D;
   const T* vb = kb + (int64_t)n_heads_kv * D;
   for (int k0 = 0; k0 < key_end; k0 += kK) {
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int key = k0 + tx * 8 + j;
-        if (tx * 8 + j >= nk || key > qpos || r >= nq) s[i][j] = -INFINITY;
+        if (tx * 8 + j >= nk || (causal && key > qpos) || r >= nq) s[i][j] = -INFINITY;
         mx = fmaxf(mx, s[i][j]);
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -148,14 +151,14 @@ __global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
 template <typename T, int D>
 int launch_prefill(const void* q, const void* cache, int64_t cbs, int64_t css, int64_t cbo,
                    const int32_t* pos_start, int64_t batch, int64_t seqlen_q, int64_t n_heads,
-                   int64_t n_heads_kv, float scale, void* out, cudaStream_t stream) {
+                   int64_t n_heads_kv, int causal, float scale, void* out, cudaStream_t stream) {
   const size_t smem = sizeof(PSmem<D>);
   auto kern = prefill_attn_kernel<T, D>;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(ceil_div(seqlen_q, kQ), (unsigned)n_heads, (unsigned)batch);
   kern<<<grid, kThreads, smem, stream>>>((const T*)q, (const T*)cache, cbs, css, cbo, pos_start,
-                                         (int)seqlen_q, (int)n_heads, (int)n_heads_kv,
+                                         (int)seqlen_q, (int)n_heads, (int)n_heads_kv, causal,
                                          scale * 1.4426950408889634f, (T*)out);
   HX_LAUNCH_CHECK("prefill_attn_kernel");
   return HX_OK;
@@ -163,23 +166,34 @@ int launch_prefill(const void* q, const void* cache, int64_t cbs, int64_t css, i
 
 }  // namespace
 
+int prefill_attention_tc(const void* q, const void* cache, int64_t cbs, int64_t css, int64_t cbo,
+                         const int32_t* pos_start, int64_t B, int64_t S, int64_t hq, int64_t hk,
+                         int64_t d, int causal, float scale, void* out, int dtype,
+                         cudaStream_t stream);
+
 extern "C" int hx_prefill_attention(const void* q, const void* cache, int64_t cache_batch_stride,
                                     int64_t cache_seq_stride, int64_t cache_batch_offset,
                                     const int32_t* pos_start, int64_t batch, int64_t seqlen_q,
                                     int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
-                                    float softmax_scale, void* out, int dtype, void* stream) {
+                                    int causal, float softmax_scale, void* out, int dtype,
+                                    void* stream) {
   HX_REQUIRE(q && cache && pos_start && out, "hx_prefill_attention: null pointer");
   HX_REQUIRE(n_heads_kv > 0 && n_heads % n_heads_kv == 0, "hx_prefill_attention: bad heads");
   HX_REQUIRE(cache_seq_stride >= 2 * n_heads_kv * head_dim, "hx_prefill_attention: bad stride");
   if (batch == 0 || seqlen_q == 0) return HX_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  // f16/bf16 with head_dim 64/128: tcgen05 kernel; everything else: the CUDA-core kernel.
+  const int tc = prefill_attention_tc(q, cache, cache_batch_stride, cache_seq_stride,
+                                      cache_batch_offset, pos_start, batch, seqlen_q, n_heads,
+                                      n_heads_kv, head_dim, causal, softmax_scale, out, dtype, s);
+  if (tc != HX_ERR_UNSUPPORTED) return tc;
 #define HX_PREFILL_CASE(DIM)                                                                  \
   case DIM:                                                                                   \
     HX_DISPATCH_DTYPE(dtype, T,                                                               \
                       return launch_prefill<T, DIM>(q, cache, cache_batch_stride,             \
                                                     cache_seq_stride, cache_batch_offset,     \
                                                     pos_start, batch, seqlen_q, n_heads,      \
-                                                    n_heads_kv, softmax_scale, out, s));      \
+                                                    n_heads_kv, causal, softmax_scale, out, s)); \
     break;
   switch (head_dim) {
     HX_PREFILL_CASE(32)

@@ -36,6 +36,12 @@ int cuda_status(cudaError_t e, const char* what);
     }                                         \
   } while (0)
 
+// Host: cached cuTensorMapEncodeTiled for a `rank`-D tensor (dims innermost first, strides in
+// bytes for dims 1..rank-1), SWIZZLE_128B, zero fill out of bounds. dtype is an hx_dtype.
+int make_tensor_map(CUtensorMap* out, const void* ptr, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, int dtype);
+int device_sm_count();
+
 #define HX_LAUNCH_CHECK(what) \
   do { int _s = hx::cuda_status(cudaGetLastError(), what); if (_s) return _s; } while (0)
 
@@ -156,6 +162,15 @@ HX_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+HX_DEVICE void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
+                           int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
 

@@ -18,11 +18,6 @@
 //   RESIDUAL  c = round(round(acc) + r)                  (block.py:155-158 residual add)
 //   SWIGLU    u = round(acc_up), g = round(acc_gate), c = round(u * round(silu(g)))
 //             (mlp.py:79-87; fc1 rows must be interleaved in blocks of 16: [up16|gate16]...)
-#include <cudaTypedefs.h>
-
-#include <mutex>
-#include <unordered_map>
-
 #include "common.cuh"
 
 namespace {
@@ -89,10 +84,13 @@ HX_DEVICE void epilogue_store(const GemmArgs& a, int m, int n0, const float* v) 
       *reinterpret_cast<uint4*>(out + c) = *reinterpret_cast<uint4*>(pack);
     }
   } else {
-    for (int j = 0; j < valid; ++j) {
-      float x = round_to<T>(v[j]);
-      if (EPI == HX_EPI_RESIDUAL) x = x + DT<T>::to_f(res[j]);
-      out[j] = DT<T>::from_f(x);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < valid) {
+        float x = round_to<T>(v[j]);
+        if (EPI == HX_EPI_RESIDUAL) x = x + DT<T>::to_f(res[j]);
+        out[j] = DT<T>::from_f(x);
+      }
     }
   }
 }
@@ -217,7 +215,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_wait_ld();
         const int n0 = n_blk * BN + c * 32;
         if (n0 >= a.N) continue;
-        const float* v = reinterpret_cast<const float*>(r);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         if (a.k_splits > 1) {
           if (m < a.M) {
             float* dst = a.ws + ((int64_t)split * a.M + m) * a.N + n0;
@@ -227,7 +227,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             } else {
-              for (int j = 0; j < valid; ++j) dst[j] = v[j];
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < valid) dst[j] = v[j];
             }
           }
         } else {
@@ -336,92 +338,17 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 // ---------------------------------------------------------------------------------------
 // Host side: tensor maps, tile selection, launch.
 // ---------------------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-struct MapKey {
-  uintptr_t ptr;
-  int64_t rows, cols, ld;
-  int box_rows, dtype, dev;
-  bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld &&
-           box_rows == o.box_rows && dtype == o.dtype && dev == o.dev;
-  }
-};
-struct MapKeyHash {
-  size_t operator()(const MapKey& k) const {
-    size_t h = std::hash<uintptr_t>()(k.ptr);
-    h ^= std::hash<int64_t>()(k.rows * 1315423911ll + k.cols * 2654435761ll + k.ld) + 0x9e3779b9 + (h << 6) + (h >> 2);
-    h ^= (size_t)(k.box_rows * 31 + k.dtype * 7 + k.dev * 131);
-    return h;
-  }
-};
-
 // 2D K-major tensor map over a [rows, cols] matrix with leading dimension ld (elements),
 // box [box_rows, 64], SWIZZLE_128B, zero fill out of bounds.
 int make_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
              int box_rows, int dtype) {
-  static std::mutex mu;
-  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  MapKey key{(uintptr_t)ptr, rows, cols, ld, box_rows, dtype, dev};
-  {
-    std::lock_guard<std::mutex> g(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-      *out = it->second;
-      return HX_OK;
-    }
-  }
-  auto fn = get_encode_fn();
-  if (!fn) {
-    hx::set_error("cuTensorMapEncodeTiled unavailable");
-    return HX_ERR_CUDA;
-  }
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUtensorMapDataType dt =
-      dtype == HX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = fn(out, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    hx::set_error("cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld", (int)r,
-                  (long long)rows, (long long)cols, (long long)ld);
-    return HX_ERR_CUDA;
-  }
-  std::lock_guard<std::mutex> g(mu);
-  if (cache.size() > 65536) cache.clear();
-  cache.emplace(key, *out);
-  return HX_OK;
+  const uint64_t dims[2] = {(uint64_t)cols, (uint64_t)rows};
+  const uint64_t strides[1] = {(uint64_t)(ld * 2)};
+  const uint32_t box[2] = {(uint32_t)BK, (uint32_t)box_rows};
+  return make_tensor_map(out, ptr, 2, dims, strides, box, dtype);
 }
 
-int device_sms() {
-  static int sms[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!sms[dev]) {
-    int n = 148;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    sms[dev] = n;
-  }
-  return sms[dev];
-}
+int device_sms() { return device_sm_count(); }
 
 struct Plan {
   int bn, m_tiles, n_tiles, k_splits, kb_per_split, k_blocks;

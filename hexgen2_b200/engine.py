@@ -1,0 +1,247 @@
+"""Engine: the prefill/decode API of hexgen2/model.py:23-124 on the B200 kernels.
+
+Same constructor, attributes and methods as the reference's native engine:
+    Engine(model_dir, engine="native", device="cuda", dtype="float16")
+    .config (HF LlamaConfig), .identity, .kind, .model
+    .prefill(input_ids, max_new_tokens) -> (LongTensor[1], {layer: Tensor[1, L, 2, hkv, d]}, logits[1, V])
+    .decode(first_token, cache, prompt_length, max_new_tokens, on_token=None) -> list[int]
+    .synchronize()
+and the same ValueError conditions. Differences that do not change results:
+  * prefill packs every layer's live cache rows with one gather kernel into one buffer that the
+    caller owns; the returned per-layer tensors are contiguous views of it;
+  * decode re-expands the received live rows into one all-layer cache with one scatter kernel;
+  * greedy argmax runs on the GPU (hx_argmax, torch.argmax tie-breaking).
+Also: Engine.from_config(...) builds a seeded random-init model of any Llama shape on the
+device (no checkpoint files), and decode_batch() runs ragged batches with per-sequence
+lengths (continuous-batching building block).
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import torch
+
+from . import ops
+from .checkpoint import (llama_config_to_gpt2_config, load_safetensors_dir, model_identity,
+                         random_native_state, remap_state_dict_hf_llama, shard_state_dict_tp)
+from .gpt import CacheState, GPTLMHeadModel
+
+
+def _check_device(device: torch.device):
+    if device.type != "cuda" or not torch.cuda.is_available():
+        raise ValueError("Native HexGen-2 on B200 requires CUDA; the CPU reference lives in the oracle")
+    major, minor = torch.cuda.get_device_capability(device)
+    if (major, minor) != (10, 0):
+        raise ValueError(f"hexgen2_b200 kernels are built for sm_100a (B200); got sm_{major}{minor}")
+
+
+class Engine:
+    def __init__(self, model_dir, engine="native", device="cuda", dtype="float16",
+                 process_group=None):
+        from transformers import LlamaConfig
+
+        self.device, self.dtype = torch.device(device), getattr(torch, dtype)
+        self.config = LlamaConfig.from_pretrained(model_dir, local_files_only=True)
+        self.identity = model_identity(model_dir)
+        scaling = getattr(self.config, "rope_scaling", None)
+        if self.config.model_type != "llama" or (
+                scaling is not None and scaling.get("rope_type", "default") != "default"):
+            raise ValueError("This baseline supports Llama architecture without RoPE scaling")
+        if engine != "native":
+            raise ValueError("hexgen2_b200 provides the native engine only; hf-reference is the "
+                             "reference's CPU validation backend")
+        self.kind = engine
+        _check_device(self.device)
+        if self.device.index is not None:
+            torch.cuda.set_device(self.device)
+        gconfig = llama_config_to_gpt2_config(self.config)
+        self.process_group = process_group
+        state = remap_state_dict_hf_llama(load_safetensors_dir(model_dir), gconfig)
+        if process_group is not None:
+            state = shard_state_dict_tp(state, gconfig, torch.distributed.get_world_size(process_group),
+                                        torch.distributed.get_rank(process_group))
+        self.model = GPTLMHeadModel(gconfig, process_group=process_group, device=self.device,
+                                    dtype=self.dtype).eval()
+        # Strict loading prevents accidental use of uninitialised weights.
+        self.model.load_state_dict(state, strict=True)
+        self._post_init()
+
+    @classmethod
+    def from_config(cls, llama_config: dict, dtype="bfloat16", device="cuda", seed=0,
+                    process_group=None):
+        """Random-init model of the given Llama shape (weights N(0, 0.02), seeded per tensor
+        name, generated on the device; every TP layout sees the same underlying weights)."""
+        from transformers import LlamaConfig
+
+        self = cls.__new__(cls)
+        self.device, self.dtype = torch.device(device), getattr(torch, dtype)
+        _check_device(self.device)
+        self.config = LlamaConfig(**llama_config)
+        self.identity = {"random_init_seed": seed}
+        self.kind = "native"
+        self.process_group = process_group
+        gconfig = llama_config_to_gpt2_config(self.config)
+        world = 1 if process_group is None else torch.distributed.get_world_size(process_group)
+        rank = 0 if process_group is None else torch.distributed.get_rank(process_group)
+        with torch.device("meta"):
+            model = GPTLMHeadModel(gconfig, process_group=process_group, dtype=self.dtype)
+        state = random_native_state(gconfig, seed=seed, dtype=self.dtype, device=self.device,
+                                    tp_world=world, tp_rank=rank)
+        model.load_state_dict(state, strict=True, assign=True)
+        self.model = model.eval()
+        self.model._rope = {}
+        self._post_init()
+        return self
+
+    def _post_init(self):
+        m = self.model
+        self.num_layers = m.n_layer
+        self.kv_heads = m.hk
+        self.head_dim = m.head_dim
+        self.row_bytes = 2 * m.hk * m.head_dim * torch.empty((), dtype=self.dtype).element_size()
+
+    # ------------------------------------------------------------------ prefill / decode
+    @torch.inference_mode()
+    def prefill(self, input_ids, max_new_tokens):
+        ids = torch.tensor([input_ids], dtype=torch.long, device=self.device)
+        L = len(input_ids)
+        state = CacheState(L + max_new_tokens)
+        logits = self.model(ids, inference_params=state, last_token_only=True).logits
+        # Send only initialized prompt positions, never the unused cache capacity.
+        cache = self.pack_live(state.key_value_memory_dict, [L])[0]
+        return ops.argmax(logits), cache, logits
+
+    def pack_live(self, caches: dict, lengths: list[int], batch_rows=None):
+        """Gathers rows [0, L_b) of cache slot b of every layer into one buffer per request.
+        Returns a list (one per request) of {layer: [1, L_b, 2, hkv, d]} contiguous views."""
+        n = self.num_layers
+        big0 = caches[0]
+        layer_stride = (caches[1].data_ptr() - big0.data_ptr()) if n > 1 else 0
+        uniform = n == 1 or all(caches[i].data_ptr() == big0.data_ptr() + i * layer_stride
+                                for i in range(n))
+        if not uniform:
+            raise ValueError("pack_live expects the engine's single all-layer cache")
+        rows = list(range(len(lengths))) if batch_rows is None else batch_rows
+        elem = big0.element_size()
+        total = sum(n * L for L in lengths)
+        packed = torch.empty(total * self.row_bytes, dtype=torch.uint8, device=self.device)
+        offs, o = [], 0
+        for L in lengths:
+            offs.append(o)
+            o += n * L * self.row_bytes
+        src = torch.tensor([big0.data_ptr() + r * big0.stride(0) * elem for r in rows],
+                           dtype=torch.int64, device=self.device)
+        live = torch.tensor(lengths, dtype=torch.int64, device=self.device)
+        dst_off = torch.tensor(offs, dtype=torch.int64, device=self.device)
+        ops.kv_pack(src, live, dst_off, n, layer_stride, big0.stride(1) * elem, self.row_bytes,
+                    max(lengths), packed)
+        out = []
+        for L, off in zip(lengths, offs):
+            view = packed[off:off + n * L * self.row_bytes].view(self.dtype).view(
+                n, 1, L, 2, self.kv_heads, self.head_dim)
+            out.append({i: view[i] for i in range(n)})
+        return out
+
+    def unpack_live(self, live_caches: list[dict], lengths: list[int], capacity: int):
+        """Scatter received live caches (one dict per request) into a fresh all-layer cache
+        [layers, B, capacity, 2, hkv, d]; returns {layer: [B, capacity, 2, hkv, d]}."""
+        n, B = self.num_layers, len(live_caches)
+        big = torch.empty(n, B, capacity, 2, self.kv_heads, self.head_dim, dtype=self.dtype,
+                          device=self.device)
+        elem = big.element_size()
+        srcs, dsts, lens = [], [], []
+        for b, (cache, L) in enumerate(zip(live_caches, lengths)):
+            for i in range(n):
+                t = cache[i]
+                if not t.is_contiguous():
+                    t = t.contiguous()
+                if t.device != self.device:
+                    t = t.to(self.device)
+                    cache[i] = t
+                srcs.append(t.data_ptr())
+                dsts.append(big[i, b].data_ptr())
+                lens.append(L)
+        base = min(srcs)
+        ops.kv_unpack(base, torch.tensor([s - base for s in srcs], dtype=torch.int64, device=self.device),
+                      torch.tensor(lens, dtype=torch.int64, device=self.device),
+                      torch.tensor(dsts, dtype=torch.int64, device=self.device), 1, 0,
+                      big.stride(2) * elem, self.row_bytes, max(lengths))
+        return {i: big[i] for i in range(n)}
+
+    @torch.inference_mode()
+    def decode(self, first_token, cache, prompt_length, max_new_tokens, on_token=None):
+        token = first_token.to(self.device).reshape(1)
+        generated = [int(token.item())]
+        if on_token:
+            on_token(generated[-1])
+        if set(cache) != set(range(self.config.num_hidden_layers)):
+            raise ValueError("KV cache does not match the configured layer count")
+        expected = (1, prompt_length, 2, self.kv_heads, self.head_dim)
+        for value in cache.values():
+            if tuple(value.shape) != expected or value.dtype != self.dtype:
+                raise ValueError("KV cache shape/dtype does not match checkpoint and prompt")
+        state = CacheState(prompt_length + max_new_tokens)
+        state.sequence_len_offset = prompt_length
+        state.key_value_memory_dict = self.unpack_live([dict(cache)], [prompt_length],
+                                                       state.max_sequence_len)
+        for _ in range(max_new_tokens - 1):
+            logits = self.model(token[:, None], inference_params=state, last_token_only=True).logits
+            state.sequence_len_offset += 1
+            token = ops.argmax(logits)
+            generated.append(int(token.item()))
+            if on_token:
+                on_token(generated[-1])
+        return generated
+
+    @torch.inference_mode()
+    def decode_batch(self, first_tokens: torch.Tensor, caches: dict, lengths: torch.Tensor,
+                     steps: int):
+        """Greedy decode of a ragged batch without host syncs: first_tokens [B] (device int64),
+        caches {layer: [B, capacity, 2, hkv, d]} holding lengths[b] live rows per sequence
+        (lengths: int32 device [B], advanced in place). Returns tokens [B, steps + 1] on the
+        device (column 0 = first_tokens)."""
+        B = first_tokens.numel()
+        capacity = caches[0].shape[1]
+        tokens = torch.empty(steps + 1, B, dtype=torch.long, device=self.device)
+        tokens[0] = first_tokens.reshape(B)
+        state = CacheState(capacity, max_batch_size=B)
+        state.key_value_memory_dict = caches
+        state.lengths_per_sample = lengths
+        for s in range(steps):
+            logits = self.model(tokens[s].view(B, 1), inference_params=state,
+                                last_token_only=True).logits
+            lengths += 1
+            ops.argmax(logits, out=tokens[s + 1])
+        return tokens.t()
+
+    @torch.inference_mode()
+    def serve_batch(self, prompts, lengths=None, max_new_tokens=16):
+        """Colocated greedy generation for a batch of requests: prompts as a list of token-id
+        lists, or a flat (ideally pinned) int64 CPU tensor plus per-request lengths. Each
+        request is prefilled straight into its slot of one all-layer cache, then the whole
+        ragged batch decodes together. Returns a list of max_new_tokens tokens per request."""
+        if isinstance(prompts, torch.Tensor):
+            flat, lens = prompts, list(lengths)
+        else:
+            lens = [len(p) for p in prompts]
+            flat = torch.tensor([t for p in prompts for t in p], dtype=torch.long)
+        B = len(lens)
+        capacity = max(lens) + max_new_tokens
+        ids = flat.to(self.device, non_blocking=True)
+        cache = self.model.allocate_inference_cache(B, capacity)
+        first = torch.empty(B, dtype=torch.long, device=self.device)
+        off = 0
+        for b, L in enumerate(lens):
+            st = CacheState(capacity, max_batch_size=B, batch_size_offset=b,
+                            key_value_memory_dict=cache)
+            logits = self.model(ids[off:off + L].view(1, L), inference_params=st,
+                                last_token_only=True).logits
+            ops.argmax(logits, out=first[b:b + 1])
+            off += L
+        lengths_dev = torch.tensor(lens, dtype=torch.int32).to(self.device, non_blocking=True)
+        toks = self.decode_batch(first, cache, lengths_dev, max_new_tokens - 1)
+        return toks.cpu().tolist()
+
+    def synchronize(self):
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)

@@ -1,0 +1,246 @@
+"""Torch-facing wrappers over the C ABI: one function per kernel entry point.
+
+Tensors are passed as raw device pointers plus sizes/strides; every launch goes on torch's
+current CUDA stream. Scratch space (split-K partials, decode split partials) comes from a
+per-device buffer that grows on demand and is reused across calls on the same stream.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import HX_EPI_NONE, HX_EPI_RESIDUAL, HX_EPI_SWIGLU, check  # noqa: F401
+
+DTYPE_CODE = {torch.float32: _lib.HX_F32, torch.float16: _lib.HX_F16, torch.bfloat16: _lib.HX_BF16}
+
+
+def _L():
+    return _lib.lib()
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("hexgen2_b200 kernels take CUDA tensors (there is no CPU path)")
+
+
+_workspaces: dict[int, torch.Tensor] = {}
+
+# Instrumentation used by bench.py: LAUNCHES counts kernels launched through this module;
+# when PROFILE is a list, every op appends (name, start_event, end_event) recorded on the
+# launching stream.
+LAUNCHES = 0
+PROFILE: list | None = None
+
+
+def _begin(name):
+    if PROFILE is None:
+        return None
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    return name, e
+
+
+def _end(tok, launches=1):
+    global LAUNCHES
+    LAUNCHES += launches
+    if tok is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        PROFILE.append((tok[0], tok[1], e))
+
+
+def workspace(nbytes: int, device=None) -> torch.Tensor | None:
+    """Per-device scratch buffer of at least nbytes (None for 0)."""
+    if nbytes == 0:
+        return None
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    buf = _workspaces.get(dev)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 0 if buf is None else buf.numel() * 2)
+        buf = torch.empty(size, dtype=torch.uint8, device=f"cuda:{dev}")
+        _workspaces[dev] = buf
+    return buf
+
+
+def reserve_workspace(nbytes: int) -> None:
+    """Grows the scratch buffer ahead of time (e.g. before CUDA-graph capture)."""
+    workspace(nbytes)
+
+
+# ----------------------------------------------------------------------------- norms
+def rmsnorm(x, weight, eps, add=None, residual_out=None, out=None, rows=None, in_stride=None):
+    """out = RMSNorm(x (+ add)) * weight, residual_out = x (+ add); rows of x at in_stride."""
+    _require_cuda(x, weight, add)
+    hidden = weight.shape[0]
+    if rows is None:
+        rows = x.numel() // hidden
+    if in_stride is None:
+        in_stride = x.stride(-2) if x.dim() >= 2 else hidden
+    if out is None:
+        out = torch.empty(rows, hidden, dtype=x.dtype, device=x.device)
+    _tok = _begin("rmsnorm")
+    check(_L().hx_rmsnorm(_p(x), _p(add), _p(residual_out), _p(out), _p(weight), rows, hidden,
+                          in_stride, out.stride(-2) if out.dim() >= 2 else hidden, float(eps),
+                          _code(x), _stream()), "hx_rmsnorm")
+    _end(_tok, 1)
+    return out
+
+
+def embed_rmsnorm(ids, table, weight, eps, residual_out, normed_out):
+    _require_cuda(ids, table)
+    _tok = _begin("embed_rmsnorm")
+    check(_L().hx_embed_rmsnorm(_p(ids), ids.numel(), _p(table), table.shape[1], _p(weight),
+                                float(eps), _p(residual_out), _p(normed_out), _code(table),
+                                _stream()), "hx_embed_rmsnorm")
+    _end(_tok, 1)
+
+
+def embedding(ids, table, vocab_start=0, out=None):
+    _require_cuda(ids, table)
+    hidden = table.shape[1]
+    if out is None:
+        out = torch.empty(ids.numel(), hidden, dtype=table.dtype, device=table.device)
+    _tok = _begin("embedding")
+    check(_L().hx_embedding(_p(ids), ids.numel(), _p(table), vocab_start, table.shape[0], hidden,
+                            _p(out), _code(table), _stream()), "hx_embedding")
+    _end(_tok, 1)
+    return out
+
+
+# ----------------------------------------------------------------------------- rotary
+def rotary_cache_write(qkv, batch, seqlen, n_heads, n_heads_kv, head_dim, pos_start, cos, sin,
+                       cache, q_out=None, batch_offset=0, interleaved=True):
+    """Rotates q/k of the packed qkv and writes k/v into cache [B, S_max, 2, hkv, d]."""
+    _require_cuda(qkv, cache, pos_start)
+    if q_out is None:
+        q_out = torch.empty(batch, seqlen, n_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+    assert cache.stride(-1) == 1 and cache.stride(-2) == head_dim and cache.stride(-3) == n_heads_kv * head_dim
+    _tok = _begin("rotary_cache_write")
+    check(_L().hx_rotary_cache_write(_p(qkv), batch, seqlen, n_heads, n_heads_kv, head_dim,
+                                     _p(pos_start), _p(cos), _p(sin), cos.shape[0],
+                                     1 if interleaved else 0, _p(q_out), _p(cache),
+                                     cache.stride(0), cache.stride(1), batch_offset,
+                                     cache.shape[1], _code(qkv), _stream()),
+          "hx_rotary_cache_write")
+    _end(_tok, 1)
+    return q_out
+
+
+# ----------------------------------------------------------------------------- gemm
+def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None):
+    """out = a @ w.T with an epilogue; a [M, K] (row-strided), w [N, K]."""
+    _require_cuda(a, w, residual)
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"gemm: shape mismatch {tuple(a.shape)} x {tuple(w.shape)}^T")
+    n_out = N // 2 if epilogue == HX_EPI_SWIGLU else N
+    if out is None:
+        out = torch.empty(M, n_out, dtype=a.dtype, device=a.device)
+    code = _code(a)
+    nbytes = _L().hx_gemm_workspace(M, N, K, epilogue, code)
+    ws = workspace(nbytes)
+    _tok = _begin("gemm")
+    check(_L().hx_gemm(_p(a), _p(w), _p(out), M, N, K, a.stride(0), w.stride(0), out.stride(0),
+                       epilogue, _p(residual), residual.stride(0) if residual is not None else 0,
+                       _p(ws), nbytes, code, _stream()), "hx_gemm")
+    _end(_tok, 2 if nbytes else 1)
+    return out
+
+
+def gemm_workspace_bytes(M, N, K, epilogue, dtype) -> int:
+    return _L().hx_gemm_workspace(M, N, K, epilogue, DTYPE_CODE[dtype])
+
+
+# ----------------------------------------------------------------------------- attention
+def prefill_attention(q, cache, pos_start, n_heads_kv, softmax_scale, causal=True, out=None,
+                      batch_offset=0):
+    """q [B, S, hq, d] against cache[batch_offset + b, :pos_start[b] + S]."""
+    _require_cuda(q, cache, pos_start)
+    B, S, hq, d = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    _tok = _begin("prefill_attention")
+    check(_L().hx_prefill_attention(_p(q), _p(cache), cache.stride(0), cache.stride(1),
+                                    batch_offset, _p(pos_start), B, S, hq, n_heads_kv, d,
+                                    1 if causal else 0, float(softmax_scale), _p(out), _code(q),
+                                    _stream()), "hx_prefill_attention")
+    _end(_tok, 1)
+    return out
+
+
+def decode_attention(q, cache, seqlens, n_heads_kv, max_seqlen, softmax_scale, out=None):
+    """q [B, hq, d] against cache[b, :seqlens[b]] (seqlens int32 on device)."""
+    _require_cuda(q, cache, seqlens)
+    B, hq, d = q.shape[0], q.shape[-2], q.shape[-1]
+    if out is None:
+        out = torch.empty(B, hq, d, dtype=q.dtype, device=q.device)
+    nbytes = _L().hx_decode_attention_workspace(B, hq, d, max_seqlen)
+    ws = workspace(nbytes)
+    _tok = _begin("decode_attention")
+    check(_L().hx_decode_attention(_p(q), _p(cache), cache.stride(0), cache.stride(1),
+                                   _p(seqlens), B, hq, n_heads_kv, d, max_seqlen,
+                                   float(softmax_scale), _p(out), _p(ws), nbytes, _code(q),
+                                   _stream()), "hx_decode_attention")
+    _end(_tok, 2 if nbytes else 1)
+    return out
+
+
+def decode_workspace_bytes(batch, n_heads, head_dim, max_seqlen) -> int:
+    return _L().hx_decode_attention_workspace(batch, n_heads, head_dim, max_seqlen)
+
+
+# ----------------------------------------------------------------------------- sampling
+def argmax(logits, out=None):
+    _require_cuda(logits)
+    rows, cols = logits.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.long, device=logits.device)
+    _tok = _begin("argmax")
+    check(_L().hx_argmax(_p(logits), rows, cols, logits.stride(0), _p(out), _code(logits),
+                         _stream()), "hx_argmax")
+    _end(_tok, 1)
+    return out
+
+
+# ----------------------------------------------------------------------------- KV handoff
+def kv_pack(src_ptrs, live_rows, dst_offsets, n_outer, outer_stride_bytes, row_stride_bytes,
+            row_bytes, max_live_rows, dst):
+    """Gather-pack of live rows (see hx_kv_pack). Pointer/length/offset arrays are int64 CUDA
+    tensors; dst may be a peer GPU's buffer given as a raw address (int)."""
+    dst_ptr = dst if isinstance(dst, int) else dst.data_ptr()
+    _tok = _begin("kv_pack")
+    check(_L().hx_kv_pack(_p(src_ptrs), _p(live_rows), _p(dst_offsets), src_ptrs.numel(),
+                          n_outer, outer_stride_bytes, row_stride_bytes, row_bytes,
+                          max_live_rows, dst_ptr, _stream()), "hx_kv_pack")
+    _end(_tok, 1)
+
+
+def kv_unpack(src, src_offsets, live_rows, dst_ptrs, n_outer, outer_stride_bytes,
+              row_stride_bytes, row_bytes, max_live_rows):
+    src_ptr = src if isinstance(src, int) else src.data_ptr()
+    _tok = _begin("kv_unpack")
+    check(_L().hx_kv_unpack(src_ptr, _p(src_offsets), _p(live_rows), _p(dst_ptrs),
+                            dst_ptrs.numel(), n_outer, outer_stride_bytes, row_stride_bytes,
+                            row_bytes, max_live_rows, _stream()), "hx_kv_unpack")
+    _end(_tok, 1)
+
+
+def device_error(clear=True) -> int:
+    return _L().hx_device_error(1 if clear else 0)

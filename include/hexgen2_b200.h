@@ -111,15 +111,17 @@ int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
 
 /* ---------------------------------------------------------------- attention */
-/* Causal prefill attention over the KV cache written by hx_rotary_cache_write.
+/* Multi-query (prefill) attention over the KV cache written by hx_rotary_cache_write.
  * q: [batch, seqlen_q, n_heads, head_dim]; keys/values are cache[cache_batch_offset + b,
- * 0 : pos_start[b] + seqlen_q]; query s of sequence b (position pos_start[b] + s) attends to
- * key positions <= pos_start[b] + s. out: [batch, seqlen_q, n_heads, head_dim].
- * Replaces flash_attn_kvpacked_func(..., causal=True) at mha.py:141/:569. */
+ * 0 : pos_start[b] + seqlen_q]. With causal != 0, query s of sequence b (position
+ * pos_start[b] + s) attends to key positions <= pos_start[b] + s (FlashAttention's bottom-right
+ * alignment); with causal == 0 every query attends to all of them (what the reference does
+ * whenever sequence_len_offset > 0, mha.py:566-568). out: [batch, seqlen_q, n_heads, head_dim].
+ * Replaces flash_attn_kvpacked_func(..., causal) at mha.py:141/:569. */
 int hx_prefill_attention(const void* q, const void* cache, int64_t cache_batch_stride,
                          int64_t cache_seq_stride, int64_t cache_batch_offset,
                          const int32_t* pos_start, int64_t batch, int64_t seqlen_q,
-                         int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
+                         int64_t n_heads, int64_t n_heads_kv, int64_t head_dim, int causal,
                          float softmax_scale, void* out, int dtype, void* stream);
 
 /* Single-query decode attention, split over the key axis (flash-decoding), GQA aware.
@@ -167,6 +169,9 @@ int hx_enable_peer_access(int peer_device);
 int hx_ipc_get_handle(const void* device_ptr, void* handle_out_64_bytes);
 int hx_ipc_open_handle(const void* handle_64_bytes, void** device_ptr_out);
 int hx_ipc_close_handle(void* device_ptr);
+/* Base address and size of the device allocation containing device_ptr (IPC handles refer to
+ * whole allocations, so a sub-range is shared as handle + offset). */
+int hx_mem_range(const void* device_ptr, void** base_out, size_t* size_out);
 /* Copy-engine peer copy (cudaMemcpyPeerAsync) of `bytes` on `stream`. */
 int hx_peer_copy(void* dst, int dst_device, const void* src, int src_device, size_t bytes,
                  void* stream);

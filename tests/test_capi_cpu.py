@@ -1,0 +1,67 @@
+"""The C-ABI library builds, loads and exports exactly what include/hexgen2_b200.h declares;
+the product path refuses to run without CUDA (no CPU fallback)."""
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "hexgen2_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(hx_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from hexgen2_b200 import _lib
+    lib = _lib.lib()
+    assert lib.hx_abi_version() == 1
+    declared = declared_symbols()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert sorted(_lib.exported_symbols()) == declared
+
+
+def test_library_symbols_are_in_the_dynamic_table():
+    import subprocess
+    from hexgen2_b200 import _lib
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True).stdout
+    exported = set(re.findall(r" T (hx_\w+)", out))
+    assert set(declared_symbols()) <= exported
+
+
+def test_workspace_queries_need_no_gpu():
+    from hexgen2_b200 import _lib
+    lib = _lib.lib()
+    assert lib.hx_gemm_workspace(1, 64, 64, 0, _lib.HX_F32) == 0
+    assert lib.hx_decode_attention_workspace(1, 32, 128, 16) == 0
+    assert lib.hx_decode_attention_workspace(1, 32, 128, 8192) > 0
+
+
+def test_ops_refuse_cpu_tensors():
+    from hexgen2_b200 import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gemm(torch.zeros(2, 8), torch.zeros(4, 8))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.rmsnorm(torch.zeros(2, 8), torch.ones(8), 1e-6)
+
+
+def test_engine_refuses_cpu(tmp_path):
+    from hexgen2_b200 import Engine
+    from hexgen2_b200.fixture import create
+    folder = create(tmp_path / "m", seed=0)
+    with pytest.raises(ValueError):
+        Engine(folder, device="cpu", dtype="float32")
+    with pytest.raises(ValueError):
+        Engine(folder, engine="hf-reference", device="cpu", dtype="float32")
+
+
+def test_graft_build_compiles_for_sm100a():
+    from hexgen2_b200 import build
+    assert "arch=compute_100a,code=sm_100a" in " ".join(build.ARCH)
+    assert build.LIB.exists()

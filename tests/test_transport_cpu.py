@@ -1,0 +1,99 @@
+"""Transport protocol on real 2-process Gloo groups (the reference's tests/test_transport.py
+cases), the packed single-message layout, and header KATs from the reference."""
+import json
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hexgen2_b200.transport import (recv_data, recv_packet, send_data, send_packet,
+                                    validate_header)
+
+
+def _worker(rank, rendezvous, packed):
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=2, init_method=Path(rendezvous).as_uri(),
+                            timeout=timedelta(seconds=30))
+    try:
+        for dtype in (torch.float16, torch.bfloat16, torch.float32):
+            cache = {7: torch.arange(-24, 24).reshape(1, 4, 2, 2, 3).to(dtype)[..., ::2],
+                     2: torch.full((1, 3, 2, 1, 4), -1.25, dtype=dtype)}
+            token = torch.tensor([42, 17], dtype=torch.long)
+            if rank == 0:
+                send_data(token, cache, dst=1, packed=packed)
+                received, returned = recv_data(src=1, num_layers=2)
+            else:
+                received, returned = recv_data(src=0, num_layers=2)
+                send_data(received, returned, dst=0, packed=packed)
+            torch.testing.assert_close(received, token, rtol=0, atol=0)
+            if list(returned) != [7, 2]:
+                raise AssertionError("Layer IDs/order changed")
+            for key in cache:
+                torch.testing.assert_close(returned[key], cache[key], rtol=0, atol=0)
+        # Empty tensors and metadata survive too.
+        if rank == 0:
+            n = send_packet({"e": torch.zeros(0, 3), "x": torch.ones(2)}, {"id": "a"}, dst=1,
+                            packed=packed)
+            assert n == 8
+        else:
+            t, meta = recv_packet(src=0)
+            assert meta == {"id": "a"} and t["e"].shape == (0, 3) and t["x"].tolist() == [1, 1]
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("packed", [False, True])
+def test_lossless_real_process_roundtrip(tmp_path, packed):
+    mp.spawn(_worker, args=(str(tmp_path / "rendezvous"), packed), nprocs=2, join=True)
+
+
+def test_invalid_metadata_is_rejected_before_allocating_payload():
+    for shape in ([-1], [True], [2 ** 40], [1] * 9):
+        with pytest.raises(ValueError):
+            validate_header({"version": 1, "tensors": [{"name": "x", "shape": shape,
+                                                        "dtype": "torch.float32"}]})
+    with pytest.raises(ValueError):
+        validate_header({"version": 1, "tensors": [
+            {"name": "x", "shape": [1], "dtype": "torch.float32"},
+            {"name": "x", "shape": [1], "dtype": "torch.float32"}]})
+    with pytest.raises(ValueError):
+        validate_header({"version": 2, "tensors": []})
+    with pytest.raises(ValueError):
+        validate_header({"version": 1, "tensors": [{"name": "x", "shape": [1], "dtype": "float"}]})
+    with pytest.raises(ValueError):
+        validate_header({"version": 1, "tensors": [{"name": str(i), "shape": [1],
+                                                    "dtype": "torch.uint8"} for i in range(1025)]})
+
+
+def test_header_bytes_match_reference(golden):
+    """The header JSON we send is byte-identical to the reference's for the pilot packet."""
+    for p in golden["transport"]:
+        h = p["header"]
+        assert validate_header(h) == p["payload_bytes"]
+        assert json.dumps(h, allow_nan=False) == p["header_utf8"]
+
+
+def _fault_worker(rank, rendezvous):
+    dist.init_process_group("gloo", rank=rank, world_size=2, init_method=Path(rendezvous).as_uri(),
+                            timeout=timedelta(seconds=30))
+    try:
+        if rank == 0:
+            # A truncated/bogus header length: the receiver must raise before allocating.
+            dist.send(torch.tensor([0], dtype=torch.int64), dst=1)
+            dist.send(torch.tensor([2 * 1024 * 1024], dtype=torch.int64), dst=1)
+        else:
+            for _ in range(2):
+                try:
+                    recv_packet(src=0)
+                    raise AssertionError("bad header accepted")
+                except ValueError:
+                    pass
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bad_header_length_rejected_on_real_ranks(tmp_path):
+    mp.spawn(_fault_worker, args=(str(tmp_path / "rv"),), nprocs=2, join=True)
