@@ -41,6 +41,9 @@ _SIGNATURES = {
                                     c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
                                     c_void_p, c_size_t, c_int, c_void_p]),
     "hx_decode_attention_workspace": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "hx_decode_attention_noalloc": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64,
+                                            c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
+                                            c_int, c_void_p]),
     "hx_argmax": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p]),
     "hx_kv_pack": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                            c_int64, c_int64, c_void_p, c_void_p]),

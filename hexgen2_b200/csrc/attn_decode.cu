@@ -13,6 +13,8 @@
 // buffered), serves all G query heads of the KV head from one copy of K/V, and writes an
 // unnormalised partial (o, m, l) per query head. A second kernel merges the splits.
 // HBM-bound: algorithmic bytes = 2 * n_heads_kv * D * L * sizeof(T) per sequence.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -314,6 +316,48 @@ int hx_decode_attention(const void* q, const void* cache, int64_t cache_batch_st
   }
 #undef HX_DECODE_CASE
   return HX_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// No-allocation variant: the split partials live in a file-scope device array.
+// ------------------------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[HX_DECODE_NOALLOC_SCRATCH_BYTES];
+
+int hx_decode_attention_noalloc(const void* q, const void* cache, int64_t cache_batch_stride,
+                                int64_t cache_seq_stride, const int32_t* seqlens_k,
+                                int64_t batch, int64_t n_heads, int64_t n_heads_kv,
+                                int64_t head_dim, int64_t max_seqlen_k, float softmax_scale,
+                                void* out, int dtype, void* stream) {
+  // In host code g_decode_noalloc_scratch names a host-side stand-in, not device memory: the
+  // device address is looked up once per device, with that device current.
+  static std::mutex mu;
+  static void* scratch_ptr[64] = {nullptr};
+  int dev = 0;
+  int s = hx::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+  if (s) return s;
+  HX_REQUIRE(dev >= 0 && dev < 64, "hx_decode_attention_noalloc: device %d out of range", dev);
+  const size_t need = hx_decode_attention_workspace(batch, n_heads, head_dim, max_seqlen_k);
+  HX_REQUIRE(need <= HX_DECODE_NOALLOC_SCRATCH_BYTES,
+             "hx_decode_attention_noalloc: this shape needs %zu bytes of split scratch, more than "
+             "the %u-byte static array (batch %lld, heads %lld, head_dim %lld, max_seqlen_k %lld)",
+             need, HX_DECODE_NOALLOC_SCRATCH_BYTES, (long long)batch, (long long)n_heads,
+             (long long)head_dim, (long long)max_seqlen_k);
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!scratch_ptr[dev]) {
+      s = hx::cuda_status(cudaGetSymbolAddress(&scratch_ptr[dev], g_decode_noalloc_scratch),
+                          "cudaGetSymbolAddress(decode scratch)");
+      if (s) {
+        scratch_ptr[dev] = nullptr;
+        return s;
+      }
+    }
+    ptr = scratch_ptr[dev];
+  }
+  return hx_decode_attention(q, cache, cache_batch_stride, cache_seq_stride, seqlens_k, batch,
+                             n_heads, n_heads_kv, head_dim, max_seqlen_k, softmax_scale, out, ptr,
+                             HX_DECODE_NOALLOC_SCRATCH_BYTES, dtype, stream);
 }
 
 }  // extern "C"

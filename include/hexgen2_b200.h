@@ -137,6 +137,29 @@ int hx_decode_attention(const void* q, const void* cache, int64_t cache_batch_st
 size_t hx_decode_attention_workspace(int64_t batch, int64_t n_heads, int64_t head_dim,
                                      int64_t max_seqlen_k);
 
+/* Scratch capacity of hx_decode_attention_noalloc (bytes, per GPU). */
+#define HX_DECODE_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* hx_decode_attention for callers that cannot allocate device memory. This entry point has no
+ * counterpart in the reference. Some callers of this library cannot call cudaMalloc: a host
+ * runtime that owns a fixed device-memory budget and hands kernels only pre-carved buffers, a
+ * process whose allocator belongs to another framework, or a latency-critical loop where an
+ * allocation (which may synchronise the device) is not allowed. They pass the same inputs and
+ * output as hx_decode_attention and no workspace: the split-KV partials go to a file-scope
+ * device array of HX_DECODE_NOALLOC_SCRATCH_BYTES (16 MiB) that every GPU which loads the
+ * library holds until the process exits. Shapes whose partials
+ * (hx_decode_attention_workspace()) exceed that are rejected with HX_ERR_INVALID. The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any CUDA-graph stream capture. All calls share the one
+ * array and nothing in it needs to start at zero (every partial is written before it is read),
+ * so calls that overlap on the GPU (different streams, concurrently) race with each other and
+ * must be serialised by the caller. Allocates nothing. */
+int hx_decode_attention_noalloc(const void* q, const void* cache, int64_t cache_batch_stride,
+                                int64_t cache_seq_stride, const int32_t* seqlens_k,
+                                int64_t batch, int64_t n_heads, int64_t n_heads_kv,
+                                int64_t head_dim, int64_t max_seqlen_k, float softmax_scale,
+                                void* out, int dtype, void* stream);
+
 /* ---------------------------------------------------------------- sampling */
 /* out_idx[r] = first index of the maximum of logits[r, 0:cols] (torch.argmax semantics).
  * Replaces logits.argmax(-1) at hexgen2/model.py:82 and :117. */
