@@ -73,10 +73,12 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index, self.rows, self.proc = index, [], None
+    def __init__(self, index: int, enabled: bool = True):
+        self.index, self.rows, self.proc, self.enabled = index, [], None, enabled
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -102,7 +104,8 @@ class ClockSampler:
 
     def summary(self) -> dict:
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None,
+                    "reasons": ["unsampled" if self.enabled else "sampling disabled (--no-clocks)"]}
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -116,19 +119,49 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------
 # Native arm, N = 1 (colocated)
 # ------------------------------------------------------------------------------------------
-def kernel_work(name_times: dict, cfg: dict, lens: list[int], out_len: int, steps: int) -> dict:
-    """Algorithmic bytes / flops per kernel class for the timed steps (for the roofline)."""
+def kernel_work(cfg: dict, lens: list[int], out_len: int, steps: int) -> dict:
+    """Algorithmic bytes / flops per kernel class over `steps` bench steps (for the roofline).
+    decode_attention: live K and V of every sequence, every layer, every decode step (+ q, out);
+    gemm_decode: every weight matrix once per decode step, plus the LM head of each prefill;
+    gemm_prefill: 2 * tokens * (layer weights) per prompt; prefill_attention: 4 * hq * d * L^2 / 2
+    per layer (causal)."""
     h, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"]
     hq, hk = cfg["num_attention_heads"], cfg["num_key_value_heads"]
     d = h // hq
     B = len(lens)
-    # Decode attention: every decode step reads the live K and V of every sequence per layer.
+    layer_params = (hq + 2 * hk) * d * h + h * hq * d + 2 * I * h + h * I
     dec_bytes = 0
     for s in range(out_len - 1):
         for Lb in lens:
             dec_bytes += 2 * hk * d * (Lb + s + 1) * 2 + 2 * hq * d * 2
-    dec_bytes *= L * steps
-    return {"decode_attention": {"bytes": dec_bytes}}
+    dec_bytes *= L
+    gemm_dec_bytes = (out_len - 1) * (L * layer_params + V * h) * 2 + B * V * h * 2
+    gemm_pre_flops = sum(2 * Lb * L * layer_params for Lb in lens)
+    attn_pre_flops = sum(4 * hq * d * Lb * Lb / 2 * L for Lb in lens)
+    return {"decode_attention": {"bytes": dec_bytes * steps},
+            "gemm_decode": {"bytes": gemm_dec_bytes * steps},
+            "gemm_prefill": {"flops": gemm_pre_flops * steps},
+            "prefill_attention": {"flops": attn_pre_flops * steps}}
+
+
+def rooflines(per_kernel: dict, work: dict, pk: dict) -> dict:
+    out = {}
+    for name, w in work.items():
+        if name not in per_kernel:
+            continue
+        ms, n = per_kernel[name]
+        if "bytes" in w:
+            achieved = w["bytes"] / (ms / 1e3) / 1e9
+            peak, unit, bound = pk["hbm_gbs"], "GB/s", "hbm"
+        else:
+            achieved = w["flops"] / (ms / 1e3) / 1e12
+            peak, unit, bound = pk["bf16_tflops"], "TFLOP/s", "tensor"
+        out[name] = {"kernel": name, "bound": bound, "achieved": round(achieved, 1), "peak": peak,
+                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": pk["source"], "launches": n, "total_ms": round(ms, 2),
+                     "avg_launch_us": round(ms * 1e3 / n, 2),
+                     "timing": "CUDA events around every launch (graph nodes inside the decode graph), instrumented pass of the timed steps"}
+    return out
 
 
 def run_native_single(args) -> dict:
@@ -150,7 +183,7 @@ def run_native_single(args) -> dict:
     lengths = torch.empty(B, dtype=torch.int32, device="cuda")
     lens_dev = torch.tensor(lens, dtype=torch.int32, device="cuda")
 
-    def one_step(ttft_events):
+    def one_step(ttft_events, use_graph=True):
         for b in range(B):
             st = CacheState(capacity, max_batch_size=B, batch_size_offset=b,
                             key_value_memory_dict=cache)
@@ -162,7 +195,7 @@ def run_native_single(args) -> dict:
         dec0 = torch.cuda.Event(enable_timing=True)
         dec1 = torch.cuda.Event(enable_timing=True)
         dec0.record()
-        toks = eng.decode_batch(first, cache, lengths, out_len - 1)
+        toks = eng.decode_batch(first, cache, lengths, out_len - 1, use_graph=use_graph)
         dec1.record()
         return toks, dec0, dec1
 
@@ -171,10 +204,11 @@ def run_native_single(args) -> dict:
     torch.cuda.synchronize()
 
     ops.LAUNCHES = 0
-    ops.PROFILE = [] if args.profile_kernels else None
     step_marks, ttfts, decs = [], [], []
-    with ClockSampler(0) as clocks:
+    with ClockSampler(0, enabled=args.clocks) as clocks:
         torch.cuda.synchronize()
+        if args.profile_region:
+            torch.cuda.cudart().cudaProfilerStart()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -188,9 +222,20 @@ def run_native_single(args) -> dict:
             decs.append((d0, d1))
         t1.record()
         torch.cuda.synchronize()
+        if args.profile_region:
+            torch.cuda.cudart().cudaProfilerStop()
     launches = ops.LAUNCHES
-    prof = ops.PROFILE
-    ops.PROFILE = None
+    # Per-kernel durations: the same steps again, every kernel bracketed by CUDA events on the
+    # launching stream; inside the decode graph the events are graph nodes and are read after
+    # each replay (so no host submission gap is ever inside a measured interval).
+    prof = None
+    if args.profile_kernels:
+        ops.PROFILE = []
+        for _ in range(args.steps):
+            one_step(None)
+        torch.cuda.synchronize()
+        prof = ops.profile_durations(ops.PROFILE)
+        ops.PROFILE = None
     total_ms = t0.elapsed_time(t1)
     dec_ms = sum(a.elapsed_time(b) for a, b in decs)
     ttft_ms = [s.elapsed_time(e) for s, evs in zip(step_marks, ttfts) for e in evs]
@@ -198,26 +243,23 @@ def run_native_single(args) -> dict:
     value = dec_tokens / (dec_ms / 1e3)
 
     # Per-kernel device time over the timed region.
-    per_kernel = {}
+    per_kernel, per_shape = {}, {}
     if prof:
-        for name, a, b in prof:
-            t = a.elapsed_time(b)
-            k = per_kernel.setdefault(name, [0.0, 0])
+        for name, t in prof:
+            k = per_shape.setdefault(name, [0.0, 0])
             k[0] += t
             k[1] += 1
-    work = kernel_work(per_kernel, cfg, lens, out_len, args.steps)
+            base = name.split("[")[0]
+            k = per_kernel.setdefault(base, [0.0, 0])
+            k[0] += t
+            k[1] += 1
+    work = kernel_work(cfg, lens, out_len, args.steps)
     pk = peaks()
-    roofline = None
-    if "decode_attention" in per_kernel:
-        ms, n = per_kernel["decode_attention"]
-        achieved = work["decode_attention"]["bytes"] / (ms / 1e3) / 1e9
-        roofline = {"kernel": "decode_attention", "bound": "hbm", "achieved": round(achieved, 1),
-                    "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                    "traffic": None, "peak_source": pk["source"],
-                    "launches": n, "avg_launch_us": round(ms * 1e3 / n, 2)}
+    roofs = rooflines(per_kernel, work, pk)
+    roofline = max(roofs.values(), key=lambda r: r["total_ms"]) if roofs else None
 
     # End to end through the public API: pinned host prompts in, host token lists out.
-    e2e = run_e2e(eng, prompts, out_len, args)
+    e2e = run_e2e(eng, prompts, out_len, args) if args.e2e_steps > 0 else None
 
     # Serial reference-algorithm baseline on the host cores (bounded sample).
     cpu = cpu_baseline(args) if args.cpu_baseline else None
@@ -232,9 +274,11 @@ def run_native_single(args) -> dict:
                    "prompt_lens_minmax": [min(lens), max(lens)], "output_len": out_len,
                    "parallelism": "colocated prefill+decode, TP1",
                    "l2": "inputs larger than L2 (13.5 GB weights + KV caches stream every step)"},
-        "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
+        "e2e": e2e, "gpu_launches": launches, "roofline": roofline, "rooflines": roofs,
         "clocks": clocks.summary(), "cpu_baseline": cpu,
         "kernel_ms": {k: round(v[0], 2) for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])},
+        "gemm_decode_us": {k.split("[")[1][:-1]: round(v[0] * 1e3 / v[1], 2)
+                           for k, v in per_shape.items() if k.startswith("gemm_decode[")},
     }
     return line
 
@@ -330,6 +374,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-profile", dest="profile_kernels", action="store_false")
+    ap.add_argument("--no-clocks", dest="clocks", action="store_false",
+                    help="do not sample nvidia-smi clocks (for runs under a profiler)")
+    ap.add_argument("--profile-region", action="store_true",
+                    help="bracket the timed region with cudaProfilerStart/Stop (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

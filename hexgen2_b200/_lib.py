@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libhexgen2_b200.so")
 
 HX_OK, HX_ERR_INVALID, HX_ERR_UNSUPPORTED, HX_ERR_CUDA, HX_ERR_DEVICE = range(5)
 HX_F32, HX_F16, HX_BF16 = 0, 1, 2
-HX_EPI_NONE, HX_EPI_RESIDUAL, HX_EPI_SWIGLU = 0, 1, 2
+HX_EPI_NONE, HX_EPI_RESIDUAL, HX_EPI_SWIGLU, HX_EPI_QKV_ROTARY = 0, 1, 2, 3
 
 _SIGNATURES = {
     "hx_abi_version": (c_int, []),
@@ -34,6 +34,10 @@ _SIGNATURES = {
                         c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_size_t, c_int,
                         c_void_p]),
     "hx_gemm_workspace": (c_size_t, [c_int64, c_int64, c_int64, c_int, c_int]),
+    "hx_gemm_qkv_rotary": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                   c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
+                                   c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                   c_void_p, c_size_t, c_int, c_void_p]),
     "hx_prefill_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
                                      c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_float,
                                      c_void_p, c_int, c_void_p]),

@@ -31,14 +31,20 @@ HX_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "me
 template <int N>
 HX_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Number of key splits; shared by the launcher and the workspace query.
-int decode_splits(int64_t batch, int64_t n_heads, int64_t max_len) {
-  const int64_t tiles = std::max<int64_t>(1, (max_len + kTile - 1) / kTile);
-  const int64_t want_ctas = 148 * 4;
+// Key splits (whole 128-key tiles); shared by the launcher and the workspace query. Splits of
+// at most 512 keys keep work items short and balanced across ragged lengths; small batches
+// split further (down to single tiles) so that ~4 items per SM exist.
+struct SplitPlan {
+  int splits, chunk;
+};
+SplitPlan decode_splits(int64_t batch, int64_t n_heads, int64_t max_len) {
+  const int64_t tiles = std::max<int64_t>(1, (max_len + 127) / 128);
   const int64_t units = std::max<int64_t>(1, batch * n_heads);
-  int64_t splits = (want_ctas + units - 1) / units;
+  int64_t splits = std::max<int64_t>((max_len + 511) / 512, (148 * 4 + units - 1) / units);
   splits = std::min<int64_t>(std::max<int64_t>(splits, 1), tiles);
-  return (int)std::min<int64_t>(splits, 1024);
+  const int64_t chunk_tiles = (tiles + splits - 1) / splits;
+  splits = (tiles + chunk_tiles - 1) / chunk_tiles;
+  return {(int)std::min<int64_t>(splits, 4096), (int)(chunk_tiles * 128)};
 }
 
 template <typename T, int D>
@@ -212,6 +218,194 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Register-resident kernel for G = n_heads / n_heads_kv <= 2 (MHA, light GQA), 16-bit dtypes.
+// Four lanes share one key row (lane s of the group reads 16-byte chunks s, s+4, ... so each
+// load instruction covers whole sectors), eight key groups per warp, two keys per group in
+// flight; every warp keeps its own online-softmax state for its keys (no __syncthreads in the
+// key loop) and the 32 partial states of a CTA are merged at the end.
+// ------------------------------------------------------------------------------------------
+constexpr int kLPK = 4;                      // lanes per key row
+constexpr int kGroups = 32 / kLPK;           // key groups per warp
+
+// kUnroll keys per key group are in flight per iteration (2 for MHA, 1 when G = 2 keeps the
+// second query's state in registers).
+template <typename T, int D, int G, int kUnroll = (G == 1 ? 2 : 1)>
+__global__ void __launch_bounds__(kThreads) decode_warp_kernel(
+    const T* __restrict__ q, const T* __restrict__ cache, int64_t cbs, int64_t css,
+    const int32_t* __restrict__ seqlens, int n_heads, int n_heads_kv, int chunk,
+    float scale_log2, T* __restrict__ out, float* __restrict__ ws_o, float* __restrict__ ws_ml,
+    int n_splits) {
+  constexpr int VPL = D / (8 * kLPK);  // 16-byte vectors per lane per row
+  constexpr int EPL = VPL * 8;          // elements per lane
+  constexpr int kWarpKeys = kGroups * kUnroll;  // keys per warp per iteration
+  __shared__ float sm_m[kThreads / 32][G], sm_l[kThreads / 32][G];
+  __shared__ float sm_acc[kThreads / 32][G][D];
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kg = lane >> 2, sl = lane & 3;
+  const int len = seqlens[b];
+  const int start = split * chunk;
+  const int end = min(start + chunk, len);
+  if (start >= end) {
+    if (n_splits > 1) {
+      for (int idx = tid; idx < G * D; idx += kThreads) {
+        const int g = idx / D, e = idx % D;
+        const int64_t slot = ((int64_t)b * n_heads + hk * G + g) * n_splits + split;
+        ws_o[slot * D + e] = 0.f;
+        if (e == 0) {
+          ws_ml[slot * 2] = -INFINITY;
+          ws_ml[slot * 2 + 1] = 0.f;
+        }
+      }
+    }
+    return;
+  }
+  // Query slice of this lane (pre-scaled into the base-2 softmax domain).
+  float qv[G][EPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const T* qr = q + ((int64_t)b * n_heads + hk * G + g) * D;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(qr + (j * kLPK + sl) * 8);
+      const T* qe = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) qv[g][j * 8 + t] = DT<T>::to_f(qe[t]) * scale_log2;
+    }
+  }
+  float m[G], l[G], acc[G][EPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) acc[g][i] = 0.f;
+  }
+  const T* kbase = cache + (int64_t)b * cbs + (int64_t)hk * D;
+  const T* vbase = kbase + (int64_t)n_heads_kv * D;
+  for (int base = start + warp * kWarpKeys; base < end; base += (kThreads / 32) * kWarpKeys) {
+    uint4 kr[kUnroll][VPL], vr[kUnroll][VPL];
+    bool valid[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int key = base + u * kGroups + kg;
+      valid[u] = key < end;
+      const int64_t off = (int64_t)key * css;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        if (valid[u]) {
+          kr[u][j] = __ldg(reinterpret_cast<const uint4*>(kbase + off + (j * kLPK + sl) * 8));
+          vr[u][j] = __ldg(reinterpret_cast<const uint4*>(vbase + off + (j * kLPK + sl) * 8));
+        } else {
+          kr[u][j] = make_uint4(0, 0, 0, 0);
+          vr[u][j] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+          const T* ke = reinterpret_cast<const T*>(&kr[u][j]);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) dot = fmaf(qv[g][j * 8 + t], DT<T>::to_f(ke[t]), dot);
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        s[u] = valid[u] ? dot : -INFINITY;
+      }
+      float mb = m[g];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) mb = fmaxf(mb, s[u]);
+      const float m_use = mb == -INFINITY ? 0.f : mb;
+      const float alpha = exp2f(m[g] - m_use);
+      float p[kUnroll], psum = 0.f;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        p[u] = exp2f(s[u] - m_use);
+        psum += p[u];
+        p[u] = round_to<T>(p[u]);
+      }
+      l[g] = l[g] * alpha + psum;
+      m[g] = mb;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          float a = acc[g][j * 8 + t] * alpha;
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u)
+            a = fmaf(p[u], DT<T>::to_f(reinterpret_cast<const T*>(&vr[u][j])[t]), a);
+          acc[g][j * 8 + t] = a;
+        }
+      }
+    }
+  }
+  // Merge the 8 key groups of the warp (lanes with equal slice index).
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = m[g];
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 8));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+    const float sc = (m[g] == -INFINITY) ? 0.f : exp2f(m[g] - M);
+    float L = l[g] * sc;
+    L += __shfl_xor_sync(0xffffffffu, L, 4);
+    L += __shfl_xor_sync(0xffffffffu, L, 8);
+    L += __shfl_xor_sync(0xffffffffu, L, 16);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      float a = acc[g][i] * sc;
+      a += __shfl_xor_sync(0xffffffffu, a, 4);
+      a += __shfl_xor_sync(0xffffffffu, a, 8);
+      a += __shfl_xor_sync(0xffffffffu, a, 16);
+      acc[g][i] = a;
+    }
+    if (kg == 0) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) sm_acc[warp][g][(j * kLPK + sl) * 8 + t] = acc[g][j * 8 + t];
+      if (sl == 0) {
+        sm_m[warp][g] = M;
+        sm_l[warp][g] = L;
+      }
+    }
+  }
+  __syncthreads();
+  // Merge the 4 warps and write the output (one split) or the split partial.
+  for (int idx = tid; idx < G * D; idx += kThreads) {
+    const int g = idx / D, e = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) M = fmaxf(M, sm_m[w][g]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+      const float mw = sm_m[w][g];
+      if (mw == -INFINITY) continue;
+      const float sc = exp2f(mw - M);
+      L += sm_l[w][g] * sc;
+      A += sm_acc[w][g][e] * sc;
+    }
+    if (n_splits == 1) {
+      out[((int64_t)b * n_heads + hk * G + g) * D + e] = DT<T>::from_f(L > 0.f ? A / L : 0.f);
+    } else {
+      const int64_t slot = ((int64_t)b * n_heads + hk * G + g) * n_splits + split;
+      ws_o[slot * D + e] = A;
+      if (e == 0) {
+        ws_ml[slot * 2] = M;
+        ws_ml[slot * 2 + 1] = L;
+      }
+    }
+  }
+}
+
 // Merge split partials: one CTA per (sequence, query head), one thread per output element.
 template <typename T, int D>
 __global__ void decode_merge_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml,
@@ -235,14 +429,23 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws_o, const float*
   }
 }
 
+}  // namespace
+
+int decode_attention_tma(const void* q, const void* cache, int64_t cbs, int64_t css,
+                         const int32_t* seqlens, int64_t batch, int64_t n_heads,
+                         int64_t n_heads_kv, int64_t head_dim, int splits, int chunk,
+                         float scale, void* out, float* ws_o, float* ws_ml, int dtype,
+                         cudaStream_t stream);
+
+namespace {
+
 template <typename T, int D>
 int launch_decode(const void* q, const void* cache, int64_t cbs, int64_t css,
                   const int32_t* seqlens, int64_t batch, int64_t n_heads, int64_t n_heads_kv,
                   int64_t max_len, float scale, void* out, void* ws, size_t ws_bytes,
                   cudaStream_t stream) {
-  const int splits = decode_splits(batch, n_heads, max_len);
-  const int64_t tiles = (max_len + kTile - 1) / kTile;
-  const int chunk = (int)(((tiles + splits - 1) / splits) * kTile);
+  const SplitPlan sp = decode_splits(batch, n_heads, max_len);
+  const int splits = sp.splits, chunk = sp.chunk;
   float* ws_o = nullptr;
   float* ws_ml = nullptr;
   if (splits > 1) {
@@ -252,16 +455,44 @@ int launch_decode(const void* q, const void* cache, int64_t cbs, int64_t css,
     ws_o = (float*)ws;
     ws_ml = ws_o + (size_t)batch * n_heads * splits * D;
   }
+  {
+    const int dt = sizeof(T) == 4 ? HX_F32 : (std::is_same<T, __half>::value ? HX_F16 : HX_BF16);
+    const int s = decode_attention_tma(q, cache, cbs, css, seqlens, batch, n_heads, n_heads_kv, D,
+                                       splits, chunk, scale, out, ws_o, ws_ml, dt, stream);
+    if (s != HX_ERR_UNSUPPORTED) {
+      if (s) return s;
+      if (splits > 1) {
+        decode_merge_kernel<T, D><<<(unsigned)(batch * n_heads), D, 0, stream>>>(ws_o, ws_ml,
+                                                                                splits, (T*)out);
+        HX_LAUNCH_CHECK("decode_merge_kernel");
+      }
+      return HX_OK;
+    }
+  }
+  dim3 grid(splits, (unsigned)n_heads_kv, (unsigned)batch);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int64_t group = n_heads / n_heads_kv;
+  bool done = false;
+  if constexpr (sizeof(T) == 2 && D >= 64) {
+    if (group <= 2) {
+      auto wk = group == 1 ? decode_warp_kernel<T, D, 1> : decode_warp_kernel<T, D, 2>;
+      wk<<<grid, kThreads, 0, stream>>>((const T*)q, (const T*)cache, cbs, css, seqlens,
+                                        (int)n_heads, (int)n_heads_kv, chunk, scale_log2,
+                                        (T*)out, ws_o, ws_ml, splits);
+      HX_LAUNCH_CHECK("decode_warp_kernel");
+      done = true;
+    }
+  }
+  if (!done) {
   const size_t smem = sizeof(Smem<T, D>);
   auto kern = decode_split_kernel<T, D>;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid(splits, (unsigned)n_heads_kv, (unsigned)batch);
-  const float scale_log2 = scale * 1.4426950408889634f;
   kern<<<grid, kThreads, smem, stream>>>((const T*)q, (const T*)cache, cbs, css, seqlens,
                                          (int)n_heads, (int)n_heads_kv, chunk, scale_log2,
                                          (T*)out, ws_o, ws_ml, splits);
   HX_LAUNCH_CHECK("decode_split_kernel");
+  }
   if (splits > 1) {
     decode_merge_kernel<T, D><<<(unsigned)(batch * n_heads), D, 0, stream>>>(ws_o, ws_ml, splits,
                                                                             (T*)out);
@@ -276,7 +507,7 @@ extern "C" {
 
 size_t hx_decode_attention_workspace(int64_t batch, int64_t n_heads, int64_t head_dim,
                                      int64_t max_seqlen_k) {
-  const int splits = decode_splits(batch, n_heads, max_seqlen_k);
+  const int splits = decode_splits(batch, n_heads, max_seqlen_k).splits;
   if (splits <= 1) return 0;
   return (size_t)batch * n_heads * splits * (head_dim + 2) * sizeof(float);
 }

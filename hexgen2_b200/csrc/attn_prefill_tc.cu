@@ -61,7 +61,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = bars + 9;
   uint64_t* o_full = bars + 10;
   uint64_t* o_empty = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* drain = bars + 12;  // MMA completion barrier used on exit
+  uint32_t* counters = reinterpret_cast<uint32_t*>(bars + 13);  // [0] kv issued [1] kv consumed [2] q consumed
+  uint32_t* tmem_slot = counters + 3;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -86,6 +88,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_full, 128);
     mbar_init(o_full, 1);
     mbar_init(o_empty, 128);
+    mbar_init(drain, 1);
+    counters[0] = counters[1] = counters[2] = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -103,6 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < L::kChunks; ++c)
         tma_load_3d(sm + L::kQ + c * kChunkBytes, &tmQ, q_full, c * 64, h, b * S + q0);
       const int bb = (int)(a.cache_batch_offset + b);
+      uint32_t issued = 0;
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
         if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) break;
@@ -114,16 +119,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(vb + c * kChunkBytes, &tmKV, &kv_full[st], c * 64, a.n_heads_kv + hk,
                       j * kRows, bb);
         }
+        ++issued;
       }
+      counters[0] = issued;
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16<T>(128, 128);
       constexpr uint32_t idesc_o = make_idesc_f16<T>(128, D, 0, 1);
       bool ok = mbar_wait(q_full, 0);
+      counters[2] = ok ? 1u : 0u;
+      uint32_t consumed = 0;
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1, sb = j & 1;
         if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
+        ++consumed;
         if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(sm + L::kQ);
@@ -159,6 +169,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(o_full);
         tc_commit(&kv_empty[st]);
       }
+      // No MMA of this CTA may still be running when TMEM is freed.
+      tc_commit(drain);
+      mbar_wait(drain, 0);
+      counters[1] = consumed;
     }
   } else {
     // Softmax / epilogue warps: row r of the tile, TMEM lane quarter = warp % 4.
@@ -174,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
       const int key0 = j * kRows;
       // Pass 1: row max over valid keys.
@@ -238,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_run = l_run * alpha + psum;
       m_run = m_new;
       // Accumulate O_j with the online rescale.
-      if (!mbar_wait(o_full, j & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(o_full, j & 1)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -265,6 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
+  __syncthreads();
+  // After an aborted wait, let issued-but-unconsumed TMA loads land (bounded) before exit.
+  if (threadIdx.x == 0) {
+    if (!counters[2]) mbar_wait(q_full, 0);
+    for (uint32_t i = counters[1]; i < counters[0]; ++i)
+      if (!mbar_wait(&kv_full[i & 1], (i >> 1) & 1)) break;
+  }
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, L::kTmemCols);

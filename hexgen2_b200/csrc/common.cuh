@@ -143,6 +143,31 @@ HX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Bounded wait by a whole warp with a warp-uniform result, for code that follows the wait with
+// warp-collective instructions (tcgen05.ld, shuffles): every lane leaves together.
+HX_DEVICE bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+// AND-reduction of a predicate over the `count` threads of named barrier `id` (warp-aligned).
+// Lets a group of warps take a common decision (e.g. all abort after a timed-out wait) so that
+// no warp is left waiting at a later named barrier.
+HX_DEVICE bool named_bar_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+HX_DEVICE void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) — tiled 2D/3D loads into this CTA's shared memory.
 // No cluster multicast anywhere in this library.

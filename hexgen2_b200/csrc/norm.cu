@@ -4,7 +4,8 @@
 //   residual = round(h + residual)                         (activation dtype)
 //   n        = round(float(residual) * rsqrt(mean(float(residual)^2) + eps))
 //   out      = round(float(n) * float(weight))
-// One CTA normalises one row; loads/stores are 16-byte vectors when the row allows it.
+// One CTA normalises one row; loads/stores are 16-byte vectors when the row allows it
+// (16-bit rows up to 8192 wide: one vector per thread, one block barrier).
 // HBM-bound: per row the kernel reads x (+add) and writes residual_out + out once.
 #include "common.cuh"
 
@@ -93,6 +94,50 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
   }
 }
 
+// One CTA per row, one 16-byte vector per thread (16-bit types, hidden a multiple of 8 up to
+// 8192): every load of the row is issued at once and there is a single block barrier, which
+// keeps latency low for the few rows of a decode step and is fully parallel for prefill rows.
+// The residual is rounded to T before it is stored, so keeping it packed in T is exact.
+template <typename T>
+__global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(
+    const T* __restrict__ x, const T* __restrict__ add, T* __restrict__ residual_out,
+    T* __restrict__ out, const T* __restrict__ weight, const int64_t* __restrict__ ids,
+    int64_t hidden, int64_t in_stride, int64_t out_stride, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const int64_t off = (int64_t)t * 8;
+  const T* xr = ids ? x + ids[row] * hidden : x + row * in_stride;
+  uint4 v = *reinterpret_cast<const uint4*>(xr + off);
+  const uint4 wv = *reinterpret_cast<const uint4*>(weight + off);
+  T* e = reinterpret_cast<T*>(&v);
+  if (add) {
+    const uint4 av = *reinterpret_cast<const uint4*>(add + row * in_stride + off);
+    const T* ae = reinterpret_cast<const T*>(&av);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) e[j] = DT<T>::from_f(DT<T>::to_f(e[j]) + DT<T>::to_f(ae[j]));
+  }
+  if (residual_out) *reinterpret_cast<uint4*>(residual_out + row * out_stride + off) = v;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float f = DT<T>::to_f(e[j]);
+    ss += f * f;
+  }
+  ss = warp_sum(ss);
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) total += red[i];
+  const float rstd = rsqrtf(total / (float)hidden + eps);
+  const T* we = reinterpret_cast<const T*>(&wv);
+  T o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    o[j] = DT<T>::from_f(round_to<T>(DT<T>::to_f(e[j]) * rstd) * DT<T>::to_f(we[j]));
+  *reinterpret_cast<uint4*>(out + row * out_stride + off) = *reinterpret_cast<const uint4*>(o);
+}
+
 template <typename T>
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const T* __restrict__ table,
                                  int64_t vocab_start, int64_t vocab_rows, int64_t hidden,
@@ -114,6 +159,15 @@ int launch_rmsnorm(const void* x, const void* add, void* residual_out, void* out
                    ((uintptr_t)x % 16 == 0) && ((uintptr_t)out % 16 == 0) &&
                    ((uintptr_t)weight % 16 == 0) && (!add || (uintptr_t)add % 16 == 0) &&
                    (!residual_out || (uintptr_t)residual_out % 16 == 0);
+  if constexpr (sizeof(T) == 2) {
+    if (vec && hidden % 256 == 0 && hidden <= 8192) {
+      rmsnorm_vec_kernel<T><<<(unsigned)rows, (unsigned)(hidden / 8), 0, stream>>>(
+          (const T*)x, (const T*)add, (T*)residual_out, (T*)out, (const T*)weight, ids, hidden,
+          in_stride, out_stride, eps);
+      HX_LAUNCH_CHECK("rmsnorm_vec_kernel");
+      return HX_OK;
+    }
+  }
   const size_t smem = (size_t)hidden * sizeof(float);
   HX_REQUIRE(smem <= 200 * 1024, "hx_rmsnorm: hidden %lld too large", (long long)hidden);
   auto kern = vec ? rmsnorm_kernel<T, true> : rmsnorm_kernel<T, false>;

@@ -63,6 +63,54 @@ __global__ void rotary_cache_kernel(const T* __restrict__ qkv, int64_t seqlen, i
   }
 }
 
+// Interleaved layout, vectorised: one thread per 16-byte chunk of the packed qkv row. A chunk
+// of q or k holds whole (x[2i], x[2i+1]) pairs, so the rotation needs only the matching
+// cos/sin entries of the same position; v chunks are copied. Grid = tokens x chunks.
+template <typename T>
+__global__ void __launch_bounds__(256) rotary_vec_kernel(
+    const T* __restrict__ qkv, int64_t n_tokens, int64_t seqlen, int n_heads, int n_heads_kv,
+    int head_dim, const int32_t* __restrict__ pos_start, const T* __restrict__ cos_t,
+    const T* __restrict__ sin_t, int64_t table_rows, T* __restrict__ q_out, T* __restrict__ cache,
+    int64_t cache_batch_stride, int64_t cache_seq_stride, int64_t cache_batch_offset,
+    int64_t cache_max_seq) {
+  constexpr int N = 16 / sizeof(T);
+  const int chunks = (n_heads + 2 * n_heads_kv) * head_dim / N;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_tokens * chunks) return;
+  const int64_t token = i / chunks;
+  const int c = (int)(i - token * chunks);
+  const int64_t b = token / seqlen, s = token - b * seqlen;
+  const int64_t pos = (int64_t)pos_start[b] + s;
+  if (pos < 0 || pos >= cache_max_seq || pos >= table_rows) {
+    record_device_error(HX_DEVERR_BAD_ARGUMENT);
+    return;
+  }
+  const int elem = c * N;
+  const int head = elem / head_dim, within = elem - head * head_dim;
+  const uint4 raw = *reinterpret_cast<const uint4*>(qkv + token * (int64_t)chunks * N + elem);
+  T* kv_dst = cache + (cache_batch_offset + b) * cache_batch_stride + pos * cache_seq_stride;
+  if (head >= n_heads + n_heads_kv) {  // v: plain copy into the cache's v slot
+    *reinterpret_cast<uint4*>(kv_dst + (int64_t)n_heads_kv * head_dim +
+                              (int64_t)(head - n_heads - n_heads_kv) * head_dim + within) = raw;
+    return;
+  }
+  const T* x = reinterpret_cast<const T*>(&raw);
+  const int half = head_dim / 2;
+  const T* cs = cos_t + pos * half + within / 2;
+  const T* sn = sin_t + pos * half + within / 2;
+  T o[N];
+#pragma unroll
+  for (int p = 0; p < N / 2; ++p) {
+    const float x0 = DT<T>::to_f(x[2 * p]), x1 = DT<T>::to_f(x[2 * p + 1]);
+    const float cv = DT<T>::to_f(cs[p]), sv = DT<T>::to_f(sn[p]);
+    o[2 * p] = DT<T>::from_f(x0 * cv - x1 * sv);
+    o[2 * p + 1] = DT<T>::from_f(x0 * sv + x1 * cv);
+  }
+  T* dst = head < n_heads ? q_out + token * (int64_t)n_heads * head_dim + elem
+                          : kv_dst + (int64_t)(head - n_heads) * head_dim + within;
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
+}
+
 }  // namespace
 
 extern "C" int hx_rotary_cache_write(const void* qkv, int64_t batch, int64_t seqlen,
@@ -80,6 +128,22 @@ extern "C" int hx_rotary_cache_write(const void* qkv, int64_t batch, int64_t seq
   HX_REQUIRE(cache_seq_stride >= 2 * n_heads_kv * head_dim, "hx_rotary_cache_write: bad stride");
   if (batch == 0 || seqlen == 0) return HX_OK;
   const int threads = 128;
+  const int esz = dtype == HX_F32 ? 4 : 2;
+  const bool vec = interleaved && (head_dim * esz) % 16 == 0 && (uintptr_t)qkv % 16 == 0 &&
+                   (uintptr_t)q_out % 16 == 0 && (uintptr_t)cache % 16 == 0 &&
+                   (cache_seq_stride * esz) % 16 == 0 && (cache_batch_stride * esz) % 16 == 0;
+  if (vec) {
+    HX_DISPATCH_DTYPE(dtype, T, {
+      const int64_t n_tokens = batch * seqlen;
+      const int64_t total = n_tokens * (n_heads + 2 * n_heads_kv) * head_dim / (16 / sizeof(T));
+      rotary_vec_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+          (const T*)qkv, n_tokens, seqlen, (int)n_heads, (int)n_heads_kv, (int)head_dim,
+          pos_start, (const T*)cos_table, (const T*)sin_table, table_rows, (T*)q_out, (T*)cache,
+          cache_batch_stride, cache_seq_stride, cache_batch_offset, cache_max_seq);
+      HX_LAUNCH_CHECK("rotary_vec_kernel");
+    });
+    return HX_OK;
+  }
   HX_DISPATCH_DTYPE(dtype, T, {
     auto kern = interleaved ? rotary_cache_kernel<T, true> : rotary_cache_kernel<T, false>;
     kern<<<(unsigned)(batch * seqlen), threads, 0, (cudaStream_t)stream>>>(

@@ -195,11 +195,16 @@ class Engine:
 
     @torch.inference_mode()
     def decode_batch(self, first_tokens: torch.Tensor, caches: dict, lengths: torch.Tensor,
-                     steps: int):
+                     steps: int, use_graph: bool = True):
         """Greedy decode of a ragged batch without host syncs: first_tokens [B] (device int64),
         caches {layer: [B, capacity, 2, hkv, d]} holding lengths[b] live rows per sequence
         (lengths: int32 device [B], advanced in place). Returns tokens [B, steps + 1] on the
-        device (column 0 = first_tokens)."""
+        device (column 0 = first_tokens).
+
+        With use_graph, the first step runs eagerly (it also sizes every scratch buffer) and one
+        single-token step is captured in a CUDA graph that is replayed for the rest: its input
+        is the static token buffer the previous replay's argmax wrote, and the length increment
+        is part of the graph, so a replay is one launch from the host."""
         B = first_tokens.numel()
         capacity = caches[0].shape[1]
         tokens = torch.empty(steps + 1, B, dtype=torch.long, device=self.device)
@@ -207,11 +212,40 @@ class Engine:
         state = CacheState(capacity, max_batch_size=B)
         state.key_value_memory_dict = caches
         state.lengths_per_sample = lengths
+        cur = torch.empty(B, 1, dtype=torch.long, device=self.device)
+        cur.copy_(tokens[0].view(B, 1))
+
+        def step():
+            logits = self.model(cur, inference_params=state, last_token_only=True).logits
+            lengths.add_(1)
+            ops.argmax(logits, out=cur.view(B))
+
+        graph = None
+        per_replay = 0
+        captured = []  # per-kernel event pairs recorded as graph nodes (profiling only)
         for s in range(steps):
-            logits = self.model(tokens[s].view(B, 1), inference_params=state,
-                                last_token_only=True).logits
-            lengths += 1
-            ops.argmax(logits, out=tokens[s + 1])
+            if graph is not None:
+                graph.replay()
+                ops.LAUNCHES += per_replay  # kernels of this library inside one replay
+            elif use_graph and s >= 1 and steps - s > 1:
+                graph = torch.cuda.CUDAGraph()
+                before = ops.LAUNCHES
+                mark = len(ops.PROFILE) if ops.PROFILE is not None else 0
+                with torch.cuda.graph(graph):
+                    step()
+                per_replay = ops.LAUNCHES - before  # counted once at capture = first replay
+                if ops.PROFILE is not None:
+                    captured = ops.PROFILE[mark:]
+                    del ops.PROFILE[mark:]
+                graph.replay()
+            else:
+                step()
+            if captured and graph is not None:
+                # Profiling: read this replay's kernel timestamps before the next replay
+                # overwrites them.
+                torch.cuda.synchronize()
+                ops.PROFILE.extend(ops.profile_durations(captured))
+            tokens[s + 1].copy_(cur.view(B))
         return tokens.t()
 
     @torch.inference_mode()

@@ -338,9 +338,14 @@ class GPTLMHeadModel(nn.Module):
         for i, layer in enumerate(layers):
             mixer, mlp = layer.mixer, layer.mlp
             cache = caches[i]
-            qkv = ops.gemm(normed, mixer.Wqkv.weight)
-            q = ops.rotary_cache_write(qkv, B, S, hq, hk, d, pos, cos, sin, cache,
-                                       batch_offset=b0, interleaved=mixer.rotary_emb_interleaved)
+            if dtype != torch.float32 and mixer.rotary_emb_interleaved:
+                q = ops.gemm_qkv_rotary(normed, mixer.Wqkv.weight, S, hq, hk, d, pos, cos, sin,
+                                        cache, batch_offset=b0).view(B, S, hq, d)
+            else:
+                qkv = ops.gemm(normed, mixer.Wqkv.weight)
+                q = ops.rotary_cache_write(qkv, B, S, hq, hk, d, pos, cos, sin, cache,
+                                           batch_offset=b0,
+                                           interleaved=mixer.rotary_emb_interleaved)
             if decode:
                 cview = cache[b0:b0 + B]
                 ctx = ops.decode_attention(q.view(B, hq, d), cview, seqlens, hk, max_pos,

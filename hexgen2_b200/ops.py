@@ -51,7 +51,9 @@ PROFILE: list | None = None
 def _begin(name):
     if PROFILE is None:
         return None
-    e = torch.cuda.Event(enable_timing=True)
+    # external=True: inside a CUDA-graph capture the record becomes an event-record node, so a
+    # replayed graph still timestamps every kernel.
+    e = torch.cuda.Event(enable_timing=True, external=True)
     e.record()
     return name, e
 
@@ -60,27 +62,34 @@ def _end(tok, launches=1):
     global LAUNCHES
     LAUNCHES += launches
     if tok is not None:
-        e = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True, external=True)
         e.record()
         PROFILE.append((tok[0], tok[1], e))
 
 
-def workspace(nbytes: int, device=None) -> torch.Tensor | None:
-    """Per-device scratch buffer of at least nbytes (None for 0)."""
+def profile_durations(entries) -> list:
+    """[(name, ms)] for PROFILE entries (event pairs must have completed)."""
+    out = []
+    for ent in entries:
+        out.append((ent[0], ent[1]) if len(ent) == 2 else (ent[0], ent[1].elapsed_time(ent[2])))
+    return out
+
+
+def workspace(nbytes: int, device=None, kind: str = "attn") -> torch.Tensor | None:
+    """Per-device scratch buffer of at least nbytes (None for 0). kind="gemm" buffers start
+    zeroed: their first 64 KiB are the GEMM's tile counters, which every completed call leaves
+    at zero, so the buffer is reused as is."""
     if nbytes == 0:
         return None
     dev = torch.cuda.current_device() if device is None else torch.device(device).index
-    buf = _workspaces.get(dev)
+    key = (dev, kind)
+    buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         size = max(nbytes, 0 if buf is None else buf.numel() * 2)
-        buf = torch.empty(size, dtype=torch.uint8, device=f"cuda:{dev}")
-        _workspaces[dev] = buf
+        alloc = torch.zeros if kind == "gemm" else torch.empty
+        buf = alloc(size, dtype=torch.uint8, device=f"cuda:{dev}")
+        _workspaces[key] = buf
     return buf
-
-
-def reserve_workspace(nbytes: int) -> None:
-    """Grows the scratch buffer ahead of time (e.g. before CUDA-graph capture)."""
-    workspace(nbytes)
 
 
 # ----------------------------------------------------------------------------- norms
@@ -155,13 +164,35 @@ def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None):
         out = torch.empty(M, n_out, dtype=a.dtype, device=a.device)
     code = _code(a)
     nbytes = _L().hx_gemm_workspace(M, N, K, epilogue, code)
-    ws = workspace(nbytes)
-    _tok = _begin("gemm")
+    ws = workspace(nbytes, kind="gemm" if code != _lib.HX_F32 else "attn")
+    _tok = _begin(f"gemm_decode[{N}x{K}]" if M <= 64 else "gemm_prefill")
     check(_L().hx_gemm(_p(a), _p(w), _p(out), M, N, K, a.stride(0), w.stride(0), out.stride(0),
                        epilogue, _p(residual), residual.stride(0) if residual is not None else 0,
                        _p(ws), nbytes, code, _stream()), "hx_gemm")
     _end(_tok, 2 if nbytes else 1)
     return out
+
+
+def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, cos, sin,
+                    cache, q_out=None, batch_offset=0):
+    """Wqkv GEMM with rotary + KV-cache write fused into its epilogue (f16/bf16): returns q
+    [rows, n_heads, head_dim]; k, v land in cache[batch_offset + b, pos_start[b] + s]."""
+    _require_cuda(x, w_qkv, cache, pos_start)
+    M, K = x.shape
+    N = w_qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty(M, n_heads, head_dim, dtype=x.dtype, device=x.device)
+    code = _code(x)
+    nbytes = _L().hx_gemm_workspace(M, N, K, _lib.HX_EPI_QKV_ROTARY, code)
+    ws = workspace(nbytes, kind="gemm")
+    _tok = _begin(f"gemm_decode[{N}x{K}]" if M <= 64 else "gemm_prefill")
+    check(_L().hx_gemm_qkv_rotary(_p(x), _p(w_qkv), M, K, x.stride(0), seqlen, n_heads,
+                                  n_heads_kv, head_dim, _p(pos_start), _p(cos), _p(sin),
+                                  cos.shape[0], _p(q_out), _p(cache), cache.stride(0),
+                                  cache.stride(1), batch_offset, cache.shape[1], _p(ws), nbytes,
+                                  code, _stream()), "hx_gemm_qkv_rotary")
+    _end(_tok, 2 if (nbytes and M > 64) else 1)
+    return q_out
 
 
 def gemm_workspace_bytes(M, N, K, epilogue, dtype) -> int:

@@ -42,7 +42,8 @@ typedef enum hx_status {
 typedef enum hx_epilogue {
   HX_EPI_NONE = 0,     /* C = round(A B^T) */
   HX_EPI_RESIDUAL = 1, /* C = round(round(A B^T) + R)   (out_proj / fc2 + residual add) */
-  HX_EPI_SWIGLU = 2    /* B rows interleaved [up16|gate16]...; C[:, j] = up_j * silu(gate_j) */
+  HX_EPI_SWIGLU = 2,   /* B rows interleaved [up16|gate16]...; C[:, j] = up_j * silu(gate_j) */
+  HX_EPI_QKV_ROTARY = 3 /* packed Wqkv output -> rotary q/k + KV-cache write (hx_gemm_qkv_rotary) */
 } hx_epilogue;
 
 /* ---------------------------------------------------------------- library / errors */
@@ -108,7 +109,25 @@ int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t
             int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
             int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
             void* stream);
+/* Workspace bytes for hx_gemm / hx_gemm_qkv_rotary. For f16/bf16 the first 64 KiB of a
+ * workspace are per-tile arrival counters of the in-kernel split reduction: they must be zero
+ * before the first call that uses the workspace and every completed call leaves them zero, so
+ * allocate the workspace zeroed once and give each concurrently running stream its own. */
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
+
+/* Wqkv projection fused with rotary and the KV-cache write: computes qkv = x * Wqkv^T
+ * ([m, (n_heads + 2*n_heads_kv) * head_dim], f32 accumulation, rounded to dtype like the
+ * reference's nn.Linear output) and, instead of storing it, writes exactly what
+ * hx_rotary_cache_write would (interleaved rotary on q and k at position pos_start[b] + s for
+ * row m = b * seqlen + s; q to q_out [m, n_heads, head_dim]; k, v to cache[cache_batch_offset
+ * + b, pos]). f16/bf16 only. Replaces mha.py:542 + :557 + :286. */
+int hx_gemm_qkv_rotary(const void* x, const void* w_qkv, int64_t m, int64_t k, int64_t ldx,
+                       int64_t seqlen, int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
+                       const int32_t* pos_start, const void* cos_table, const void* sin_table,
+                       int64_t table_rows, void* q_out, void* cache, int64_t cache_batch_stride,
+                       int64_t cache_seq_stride, int64_t cache_batch_offset,
+                       int64_t cache_max_seq, void* workspace, size_t workspace_bytes, int dtype,
+                       void* stream);
 
 /* ---------------------------------------------------------------- attention */
 /* Multi-query (prefill) attention over the KV cache written by hx_rotary_cache_write.

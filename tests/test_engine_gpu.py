@@ -8,10 +8,12 @@ in the reference's own acceptance form |a - b| <= atol + rtol * |b| with atol = 
 for every logit. At full architecture width it cannot hold for every logit in bf16, for any
 implementation that does not reproduce cuBLAS's and FlashAttention's exact f32 summation order:
 two restatements of the reference itself (its CPU torch attention vs FlashAttention numerics)
-already differ by up to 0.043 (TinyLlama width) and 0.086 (7B width) after two layers. There
-the asserted bar is: the max error is within max(2e-2, the reference's own spread), at least
-98% of logits are within 2e-2 (atol = rtol form), and greedy tokens are identical except at a
-near-tie of the reference's own logits (top-2 margin inside the tolerance), which is reported.
+already differ by up to 0.043 (TinyLlama width) and 0.086-0.107 (7B width) after two layers,
+with only ~70% of 7B-width logits within 2e-2 of each other. There the asserted bar is: the
+max error is within max(2e-2, the reference's own spread), the fraction of logits within 2e-2
+(atol = rtol form) is at least the reference's own (capped at 99%), and greedy tokens are
+identical except at a near-tie of the reference's own logits (top-2 margin inside the
+tolerance), which is reported.
 """
 import pytest
 import torch
@@ -108,10 +110,12 @@ def _teacher_forced_check(oracle, eng, prompt, steps, tol, noise_oracle=None):
         diff = (got - ref).abs()
         err = diff.max().item()
         within = (diff <= tol + tol * ref.abs()).float().mean().item()
-        print(f"max |logit err| {err:.4f}; reference's own bf16 spread {floor:.4f}; "
-              f"{within:.4%} of logits within {tol}")
+        n_diff = (n_logits[0].float() - ref).abs()
+        within_floor = (n_diff <= tol + tol * ref.abs()).float().mean().item()
+        print(f"max |logit err| {err:.4f} (reference's own spread {floor:.4f}); "
+              f"{within:.4%} of logits within {tol} (reference vs itself: {within_floor:.4%})")
         assert err <= max(floor, tol), (err, floor)
-        assert within >= 0.98, within
+        assert within >= min(within_floor, 0.99), (within, within_floor)
     ties = []
     ids = torch.tensor([prompt + tokens[:-1]])
     full = oracle.forward(ids, None, last_token_only=False)[0].float()
