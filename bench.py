@@ -276,6 +276,7 @@ def run_native_single(args) -> dict:
                    "l2": "inputs larger than L2 (13.5 GB weights + KV caches stream every step)"},
         "e2e": e2e, "gpu_launches": launches, "roofline": roofline, "rooflines": roofs,
         "clocks": clocks.summary(), "cpu_baseline": cpu,
+        "decode_ms_per_step": [round(a.elapsed_time(b), 2) for a, b in decs],
         "kernel_ms": {k: round(v[0], 2) for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])},
         "gemm_decode_us": {k.split("[")[1][:-1]: round(v[0] * 1e3 / v[1], 2)
                            for k, v in per_shape.items() if k.startswith("gemm_decode[")},
@@ -362,8 +363,127 @@ def run_reference(args) -> dict:
                     "d2h_bytes_per_step": 0}}
 
 
+# ------------------------------------------------------------------------------------------
+# Single-kernel mode (--kernel): one entry point alone at one shape, for roofline numbers and
+# for ncu captures that must stay small (a few GB on the device).
+# ------------------------------------------------------------------------------------------
+def run_kernel(args) -> dict:
+    from hexgen2_b200 import ops
+
+    torch.cuda.set_device(0)
+    pk = peaks()
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    dt = torch.bfloat16
+    l2 = 126 * 2 ** 20
+    iters = args.iters
+
+    def timed(fn, n):
+        # Warm-up launches size every scratch buffer; the timed launches are captured in one
+        # CUDA graph so host-side launch cost is not part of the per-kernel time.
+        for i in range(5):
+            fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(n):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        graph.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) * 1e3 / n  # us per call
+
+    if args.kernel == "gemm":
+        M, N, K = (int(v) for v in args.shape.split(","))
+        epi = {"none": ops.HX_EPI_NONE, "residual": ops.HX_EPI_RESIDUAL,
+               "swiglu": ops.HX_EPI_SWIGLU}[args.epi]
+        wbytes = N * K * 2
+        copies = max(1, min(64, -(-3 * l2 // wbytes)))  # weights rotate through > L2
+        ws = [torch.randn(N, K, generator=g, device="cuda", dtype=dt) * 0.02 for _ in range(copies)]
+        x = torch.randn(M, K, generator=g, device="cuda", dtype=dt)
+        n_out = N // 2 if epi == ops.HX_EPI_SWIGLU else N
+        out = torch.empty(M, n_out, device="cuda", dtype=dt)
+        res = torch.randn(M, n_out, generator=g, device="cuda", dtype=dt) if epi == ops.HX_EPI_RESIDUAL else None
+        us = timed(lambda i: ops.gemm(x, ws[i % copies], epi, residual=res, out=out), iters)
+        nbytes = wbytes + M * K * 2 + M * n_out * 2 * (2 if res is not None else 1)
+        flops = 2 * M * N * K
+        gbs, tfs = nbytes / us / 1e3, flops / us / 1e6
+        bound = "hbm" if M <= 64 else "tensor"
+        achieved, peak = (gbs, pk["hbm_gbs"]) if bound == "hbm" else (tfs, pk["bf16_tflops"])
+        return {"kernel": f"gemm {args.epi}", "shape": [M, N, K], "us": round(us, 2),
+                "GB/s": round(gbs, 1), "TFLOP/s": round(tfs, 1), "bound": bound,
+                "frac": round(achieved / peak, 4), "peak_source": pk["source"],
+                "l2": f"{copies} weight copies rotated"}
+    if args.kernel == "decode_attention":
+        # L = live keys of every sequence, or with --ragged the mean of the bench's lognormal
+        # prompt lengths plus L (mid-decode), one length per sequence.
+        B, hq, hk, d, L = (int(v) for v in args.shape.split(","))
+        lens_l = [Lp + L for Lp in prompt_lengths(B, args.seed)] if args.ragged else [L] * B
+        cap = max(lens_l) + 128
+        cache = torch.randn(B, cap, 2, hk, d, generator=g, device="cuda", dtype=dt)
+        q = torch.randn(B, hq, d, generator=g, device="cuda", dtype=dt)
+        lens = torch.tensor(lens_l, dtype=torch.int32, device="cuda")
+        out = torch.empty(B, hq, d, device="cuda", dtype=dt)
+        us = timed(lambda i: ops.decode_attention(q, cache, lens, hk, cap, d ** -0.5, out=out), iters)
+        nbytes = sum(lens_l) * 2 * hk * d * 2 + 2 * B * hq * d * 2
+        gbs = nbytes / us / 1e3
+        return {"kernel": "decode_attention", "shape": [B, hq, hk, d, L], "ragged": args.ragged,
+                "mean_len": round(sum(lens_l) / B, 1), "us": round(us, 2),
+                "GB/s": round(gbs, 1), "bound": "hbm", "frac": round(gbs / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"],
+                "l2": f"cache {cache.numel() * 2 / 2 ** 20:.0f} MiB vs 126 MiB L2"}
+    if args.kernel == "prefill_attention":
+        B, hq, hk, d, S = (int(v) for v in args.shape.split(","))
+        cache = torch.randn(B, S, 2, hk, d, generator=g, device="cuda", dtype=dt)
+        q = torch.randn(B, S, hq, d, generator=g, device="cuda", dtype=dt)
+        pos = torch.zeros(B, dtype=torch.int32, device="cuda")
+        out = torch.empty_like(q)
+        us = timed(lambda i: ops.prefill_attention(q, cache, pos, hk, d ** -0.5, out=out), iters)
+        flops = 4 * B * hq * d * S * S / 2
+        tfs = flops / us / 1e6
+        return {"kernel": "prefill_attention", "shape": [B, hq, hk, d, S], "us": round(us, 2),
+                "TFLOP/s": round(tfs, 1), "bound": "tensor",
+                "frac": round(tfs / pk["bf16_tflops"], 4), "peak_source": pk["source"]}
+    if args.kernel == "kv_pack":
+        layers, hk, d, L, B = (int(v) for v in args.shape.split(","))
+        cap = L + 64
+        row = 2 * hk * d * 2
+        big = torch.randn(layers, B, cap, 2, hk, d, generator=g, device="cuda", dtype=dt)
+        dst = torch.empty(B * layers * L * row, dtype=torch.uint8, device="cuda")
+        elem = 2
+        src = torch.tensor([big.data_ptr() + b * big.stride(1) * elem for b in range(B)],
+                           dtype=torch.int64, device="cuda")
+        live = torch.full((B,), L, dtype=torch.int64, device="cuda")
+        offs = torch.tensor([b * layers * L * row for b in range(B)], dtype=torch.int64, device="cuda")
+        us = timed(lambda i: ops.kv_pack(src, live, offs, layers, big.stride(0) * elem,
+                                         big.stride(2) * elem, row, L, dst), iters)
+        nbytes = 2 * B * layers * L * row
+        gbs = nbytes / us / 1e3
+        return {"kernel": "kv_pack", "shape": [layers, hk, d, L, B], "us": round(us, 2),
+                "GB/s": round(gbs, 1), "bound": "hbm", "frac": round(gbs / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"]}
+    raise ValueError(args.kernel)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--kernel", choices=["gemm", "decode_attention", "prefill_attention", "kv_pack"],
+                    help="time one kernel alone (shape via --shape) instead of the model step")
+    ap.add_argument("--shape", default="32,4096,4096",
+                    help="gemm: M,N,K; decode_attention: B,hq,hkv,d,L; prefill_attention: "
+                         "B,hq,hkv,d,S; kv_pack: layers,hkv,d,L,B")
+    ap.add_argument("--epi", choices=["none", "residual", "swiglu"], default="none")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--workload", choices=["serve", "kv_handoff"], default="serve",
+                    help="kv_handoff: the KV-cache handoff microbenchmark (70B cache geometry)")
+    ap.add_argument("--kv-batches", default="1,8,64",
+                    help="kv_handoff: requests per transfer, comma separated")
+    ap.add_argument("--ragged", action="store_true",
+                    help="decode_attention: per-sequence lengths = bench prompt lengths + L")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
@@ -381,13 +501,18 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.kernel:
+        line = run_kernel(args)
+    elif args.workload == "kv_handoff" and args.impl == "native":
+        from hexgen2_b200.disagg import run_kv_bench
+        line = run_kv_bench(args, sys.modules[__name__])
+    elif args.impl == "reference":
         line = run_reference(args)
     elif args.gpus == 1:
         line = run_native_single(args)
     else:
         from hexgen2_b200.disagg import run_bench_disaggregated
-        line = run_bench_disaggregated(args)
+        line = run_bench_disaggregated(args, sys.modules[__name__])
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -16,6 +16,8 @@ HX_DEVICE void better(float& bv, int64_t& bi, float v, int64_t i) {
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ logits, int64_t cols, int64_t ld,
                               int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const T* row = logits + (int64_t)blockIdx.x * ld;
   float bv = -INFINITY;
   int64_t bi = cols;  // sentinel larger than any index
@@ -47,8 +49,11 @@ extern "C" int hx_argmax(const void* logits, int64_t rows, int64_t cols, int64_t
   HX_REQUIRE(logits && out_idx && cols > 0 && ld >= cols, "hx_argmax: bad arguments");
   if (rows == 0) return HX_OK;
   HX_DISPATCH_DTYPE(dtype, T, {
-    argmax_kernel<T><<<(unsigned)rows, 1024, 0, (cudaStream_t)stream>>>((const T*)logits, cols,
-                                                                        ld, out_idx);
+    const int s = hx::cuda_status(
+        launch_ex(argmax_kernel<T>, dim3((unsigned)rows), dim3(1024), 0, (cudaStream_t)stream, 1,
+                  (const T*)logits, cols, ld, out_idx),
+        "argmax_kernel launch");
+    if (s) return s;
     HX_LAUNCH_CHECK("argmax_kernel");
   });
   return HX_OK;

@@ -433,9 +433,9 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws_o, const float*
 
 int decode_attention_tma(const void* q, const void* cache, int64_t cbs, int64_t css,
                          const int32_t* seqlens, int64_t batch, int64_t n_heads,
-                         int64_t n_heads_kv, int64_t head_dim, int splits, int chunk,
-                         float scale, void* out, float* ws_o, float* ws_ml, int dtype,
-                         cudaStream_t stream);
+                         int64_t n_heads_kv, int64_t head_dim, float scale, void* out, void* ws,
+                         size_t ws_bytes, int dtype, cudaStream_t stream);
+size_t decode_tma_workspace(int64_t batch, int64_t n_heads, int64_t head_dim);
 
 namespace {
 
@@ -444,6 +444,13 @@ int launch_decode(const void* q, const void* cache, int64_t cbs, int64_t css,
                   const int32_t* seqlens, int64_t batch, int64_t n_heads, int64_t n_heads_kv,
                   int64_t max_len, float scale, void* out, void* ws, size_t ws_bytes,
                   cudaStream_t stream) {
+  {
+    // Main path (f16/bf16, head_dim 64/128, <= 2 query heads per KV head): balanced TMA kernel.
+    const int dt = sizeof(T) == 4 ? HX_F32 : (std::is_same<T, __half>::value ? HX_F16 : HX_BF16);
+    const int s = decode_attention_tma(q, cache, cbs, css, seqlens, batch, n_heads, n_heads_kv, D,
+                                       scale, out, ws, ws_bytes, dt, stream);
+    if (s != HX_ERR_UNSUPPORTED) return s;
+  }
   const SplitPlan sp = decode_splits(batch, n_heads, max_len);
   const int splits = sp.splits, chunk = sp.chunk;
   float* ws_o = nullptr;
@@ -454,20 +461,6 @@ int launch_decode(const void* q, const void* cache, int64_t cbs, int64_t css,
                ws_bytes, need);
     ws_o = (float*)ws;
     ws_ml = ws_o + (size_t)batch * n_heads * splits * D;
-  }
-  {
-    const int dt = sizeof(T) == 4 ? HX_F32 : (std::is_same<T, __half>::value ? HX_F16 : HX_BF16);
-    const int s = decode_attention_tma(q, cache, cbs, css, seqlens, batch, n_heads, n_heads_kv, D,
-                                       splits, chunk, scale, out, ws_o, ws_ml, dt, stream);
-    if (s != HX_ERR_UNSUPPORTED) {
-      if (s) return s;
-      if (splits > 1) {
-        decode_merge_kernel<T, D><<<(unsigned)(batch * n_heads), D, 0, stream>>>(ws_o, ws_ml,
-                                                                                splits, (T*)out);
-        HX_LAUNCH_CHECK("decode_merge_kernel");
-      }
-      return HX_OK;
-    }
   }
   dim3 grid(splits, (unsigned)n_heads_kv, (unsigned)batch);
   const float scale_log2 = scale * 1.4426950408889634f;
@@ -507,9 +500,15 @@ extern "C" {
 
 size_t hx_decode_attention_workspace(int64_t batch, int64_t n_heads, int64_t head_dim,
                                      int64_t max_seqlen_k) {
+  // The larger of the two paths' needs: the balanced TMA kernel (f16/bf16, head_dim 64/128) and
+  // the fixed-split kernels (other shapes and dtypes).
+  if (batch <= 0 || n_heads <= 0 || head_dim <= 0 || max_seqlen_k <= 0) return 0;
   const int splits = decode_splits(batch, n_heads, max_seqlen_k).splits;
-  if (splits <= 1) return 0;
-  return (size_t)batch * n_heads * splits * (head_dim + 2) * sizeof(float);
+  const size_t split_need =
+      splits <= 1 ? 0 : (size_t)batch * n_heads * splits * (head_dim + 2) * sizeof(float);
+  const size_t tma_need =
+      (head_dim == 64 || head_dim == 128) ? decode_tma_workspace(batch, n_heads, head_dim) : 0;
+  return std::max(split_need, tma_need);
 }
 
 int hx_decode_attention(const void* q, const void* cache, int64_t cache_batch_stride,

@@ -1,10 +1,15 @@
-// K5 (main path): persistent TMA-fed split-KV decode attention for f16/bf16, head_dim 64/128,
-// up to 2 query heads per KV head (MHA and light GQA). Semantics and numerics are those of
+// K5 (main path): persistent TMA-fed decode attention for f16/bf16, head_dim 64/128, up to 2
+// query heads per KV head (MHA and light GQA). Semantics and numerics are those of
 // attn_decode.cu (flash_attn_kvpacked_func with q_len 1, FlashAttention-2 rounding points).
 //
-// Work items are (sequence, kv head, key split) with splits of a whole number of 128-key
-// tiles; each CTA (one per SM) walks items i = blockIdx.x, +gridDim.x, ... and skips the empty
-// ones (split start >= the sequence's length, read from seqlens on the device).
+// Balanced partition. The live keys of every (sequence, kv head) pair form a run of 128-key
+// tiles; the runs of all pairs, sequence-major, make one list of T tiles (T is computed on the
+// device from seqlens, so ragged batches inside a CUDA graph need no host work). CTA c of G
+// (one per SM) takes tiles [c*T/G, (c+1)*T/G): every CTA streams the same number of KV bytes
+// whatever the length mix. A run that lies wholly inside one CTA's range is finished by that CTA
+// (output written directly). A run cut by a range boundary leaves one partial (o, m, l) per
+// contributing CTA: the CTA where the run ends in the middle of writes slot 2c + 1, the CTAs
+// where it continues write slot 2c, and decode_tma_merge_kernel combines them in CTA order.
 //   warp 0      TMA producer: K and V boxes [128 keys x 64 elements] (SWIZZLE_128B) straight
 //               out of the cache ([B, max_seq, 2*hkv, d] as a 4D tensor map) into a ring of
 //               64 KB (d=128) stages; ~192 KB stay in flight per SM, which is what keeps HBM busy.
@@ -13,8 +18,7 @@
 //               different 16-byte slots, so no bank conflicts) against q held in shared memory;
 //               online softmax across the warp with shuffles; PV: for each valid key, the warp
 //               reads that V row (lane = 4 (or 2) output dims) and accumulates.
-//               Each warp keeps its own (m, l, o); the four are merged at the item's end and
-//               written as the output (one split) or as a split partial.
+//               Each warp keeps its own (m, l, o); the four are merged at the run's end.
 // Cache rows past a sequence's length are never used: their scores are masked and P.V stops
 // at the last valid key, so stale cache bits cannot leak in.
 #include "common.cuh"
@@ -25,6 +29,7 @@ constexpr int kTileKeys = 128;
 constexpr int kBoxBytes = kTileKeys * 128;  // [128 keys x 64 elements] swizzled box
 constexpr int kConsumers = 4;
 constexpr int kThreadsTma = 32 * (1 + kConsumers);
+constexpr int kMaxSeqs = 2048;              // sequences per call (tile prefix kept in smem)
 
 template <int D>
 struct DLay {
@@ -37,16 +42,66 @@ struct DLay {
 struct DecArgs {
   const void* q;
   void* out;
-  float* ws_o;
-  float* ws_ml;
+  float* ws_o;   // [2 * grid][G][D] partial outputs
+  float* ws_ml;  // [2 * grid][G][2] partial (m, l)
+  int* ws_pre;   // [batch + 1] tile prefix (written by CTA 0 for the merge kernel)
   const int32_t* seqlens;
-  int n_heads, n_heads_kv, batch, splits, chunk;
+  int n_heads, n_heads_kv, batch, max_seq;
   float scale_log2;
 };
 
 HX_DEVICE void named_barrier_consumers() {
   asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumers) : "memory");
 }
+
+HX_DEVICE int live_len(const DecArgs& a, int b) {
+  return min(max(a.seqlens[b], 0), a.max_seq);
+}
+
+// First CTA (of `grid`) whose tile range [c*T/grid, (c+1)*T/grid) contains tile u.
+HX_DEVICE int cta_of(int64_t u, int64_t T, int grid) {
+  return (int)(((u + 1) * grid - 1) / T);
+}
+
+// One run piece of this CTA's range: sequence b, kv head hk, tiles [t_lo, t_hi) of the run,
+// run bounds [seg0, seg1) in the global tile list.
+struct Piece {
+  int b, hk, t_lo, t_hi;
+  int64_t seg0, seg1;
+};
+
+// Walks the pieces of [u0, u1) in order; `pre` is the per-sequence prefix of tiles x hkv.
+struct PieceWalker {
+  const int* pre;
+  int hkv, b;
+  int64_t u, u1;
+  HX_DEVICE PieceWalker(const int* pre_, int hkv_, int batch, int64_t u0, int64_t u1_)
+      : pre(pre_), hkv(hkv_), b(0), u(u0), u1(u1_) {
+    // Largest b with pre[b] <= u0 (binary search over the monotone prefix).
+    int lo = 0, hi = batch;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (pre[mid] <= u0) lo = mid; else hi = mid - 1;
+    }
+    b = lo;
+  }
+  HX_DEVICE bool next(Piece& p) {
+    if (u >= u1) return false;
+    while (pre[b + 1] <= u) ++b;
+    const int tiles = (pre[b + 1] - pre[b]) / hkv;
+    const int64_t rel = u - pre[b];
+    const int hk = (int)(rel / tiles);
+    p.b = b;
+    p.hk = hk;
+    p.seg0 = pre[b] + (int64_t)hk * tiles;
+    p.seg1 = p.seg0 + tiles;
+    const int64_t e = p.seg1 < u1 ? p.seg1 : u1;
+    p.t_lo = (int)(u - p.seg0);
+    p.t_hi = (int)(e - p.seg0);
+    u = e;
+    return true;
+  }
+};
 
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(kThreadsTma, 1)
@@ -59,10 +114,10 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
   float* ml = mo + kConsumers * G * D;                                    // [4][G][2]
   uint64_t* full = reinterpret_cast<uint64_t*>(ml + kConsumers * G * 2 + 2);
   uint64_t* empty = full + L::kStages;
+  int* pre = reinterpret_cast<int*>(empty + L::kStages);                  // [batch + 1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hkv = a.n_heads_kv;
-  const int total_items = a.batch * hkv * a.splits;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmKV);
@@ -72,20 +127,41 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
     }
     fence_mbar_init();
   }
+  pdl_wait();  // q, the cache rows and seqlens come from earlier kernels
+  pdl_trigger();
+  if (warp == 1) {
+    // Tile prefix over sequences: pre[b] = hkv * sum_{b' < b} ceil(len_b' / 128).
+    int carry = 0;
+    if (lane == 0) pre[0] = 0;
+    for (int base = 0; base < a.batch; base += 32) {
+      const int b = base + lane;
+      int v = b < a.batch ? hkv * ((live_len(a, b) + kTileKeys - 1) / kTileKeys) : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      if (b < a.batch) pre[b + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
   __syncthreads();
+  const int64_t total = pre[a.batch];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i <= a.batch; i += blockDim.x) a.ws_pre[i] = pre[i];
+  if (total == 0) return;
+  const int64_t u0 = (int64_t)blockIdx.x * total / gridDim.x;
+  const int64_t u1 = (int64_t)(blockIdx.x + 1) * total / gridDim.x;
+  if (u0 >= u1) return;
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0, issued = 0;
-      for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-        const int split = item % a.splits;
-        const int hk = (item / a.splits) % hkv;
-        const int b = item / (a.splits * hkv);
-        const int len = a.seqlens[b];
-        const int start = split * a.chunk;
-        const int end = min(start + a.chunk, len);
-        for (int key0 = start; key0 < end; key0 += kTileKeys) {
+      PieceWalker w(pre, hkv, a.batch, u0, u1);
+      Piece p;
+      while (w.next(p)) {
+        for (int t = p.t_lo; t < p.t_hi; ++t) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) goto producer_done;
           ++issued;
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
@@ -93,8 +169,8 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
           uint8_t* vb = kb + L::kChunks * kBoxBytes;
 #pragma unroll
           for (int c = 0; c < L::kChunks; ++c) {
-            tma_load_4d(kb + c * kBoxBytes, &tmKV, &full[stage], c * 64, hk, key0, b);
-            tma_load_4d(vb + c * kBoxBytes, &tmKV, &full[stage], c * 64, hkv + hk, key0, b);
+            tma_load_4d(kb + c * kBoxBytes, &tmKV, &full[stage], c * 64, p.hk, t * kTileKeys, p.b);
+            tma_load_4d(vb + c * kBoxBytes, &tmKV, &full[stage], c * 64, hkv + p.hk, t * kTileKeys, p.b);
           }
           if (++stage == L::kStages) {
             stage = 0;
@@ -120,29 +196,15 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
   int stage = 0;
   uint32_t phase = 0;
   bool ok = true;
-  // Every consumer warp walks the same item / tile / barrier sequence even after a failed
+  // Every consumer warp walks the same piece / tile / barrier sequence even after a failed
   // (timed-out) wait, only skipping the work, so no warp is left waiting at a named barrier.
-  for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-    const int split = item % a.splits;
-    const int hk = (item / a.splits) % hkv;
-    const int b = item / (a.splits * hkv);
-    const int len = a.seqlens[b];
-    const int start = split * a.chunk;
-    const int end = min(start + a.chunk, len);
-    if (start >= end) {
-      if (a.splits > 1) {
-        for (int idx = ct; idx < G * D; idx += 32 * kConsumers) {
-          const int g = idx / D, e = idx % D;
-          const int64_t slot = ((int64_t)b * a.n_heads + hk * G + g) * a.splits + split;
-          a.ws_o[slot * D + e] = 0.f;
-          if (e == 0) {
-            a.ws_ml[slot * 2] = -INFINITY;
-            a.ws_ml[slot * 2 + 1] = 0.f;
-          }
-        }
-      }
-      continue;
-    }
+  PieceWalker walker(pre, hkv, a.batch, u0, u1);
+  Piece pc;
+  while (walker.next(pc)) {
+    const int b = pc.b, hk = pc.hk;
+    const int len = live_len(a, b);
+    const int start = pc.t_lo * kTileKeys;
+    const int end = min(pc.t_hi * kTileKeys, len);
     for (int idx = ct; idx < G * D; idx += 32 * kConsumers) {
       const int g = idx / D, e = idx % D;
       q_s[g * D + e] = DT<T>::to_f(reinterpret_cast<const T*>(a.q)[((int64_t)b * a.n_heads + hk * G + g) * D + e]) * a.scale_log2;
@@ -288,6 +350,8 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
       }
     }
     named_barrier_consumers();
+    const bool whole = pc.seg0 >= u0 && pc.seg1 <= u1;
+    const int64_t slot = 2 * (int64_t)blockIdx.x + (pc.seg0 < u0 ? 0 : 1);
     for (int idx = ct; ok && idx < G * D; idx += 32 * kConsumers) {
       const int g = idx / D, e = idx % D;
       float M = -INFINITY;
@@ -302,15 +366,14 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
         Ls += ml[(w * G + g) * 2 + 1] * sc;
         A += mo[(w * G + g) * D + e] * sc;
       }
-      const int64_t h = (int64_t)b * a.n_heads + hk * G + g;
-      if (a.splits == 1) {
+      if (whole) {
+        const int64_t h = (int64_t)b * a.n_heads + hk * G + g;
         reinterpret_cast<T*>(a.out)[h * D + e] = DT<T>::from_f(Ls > 0.f ? A / Ls : 0.f);
       } else {
-        const int64_t slot = h * a.splits + split;
-        a.ws_o[slot * D + e] = A;
+        a.ws_o[(slot * G + g) * D + e] = A;
         if (e == 0) {
-          a.ws_ml[slot * 2] = M;
-          a.ws_ml[slot * 2 + 1] = Ls;
+          a.ws_ml[(slot * G + g) * 2] = M;
+          a.ws_ml[(slot * G + g) * 2 + 1] = Ls;
         }
       }
     }
@@ -318,12 +381,48 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
   }
 }
 
+// Combines the partials of runs that were cut by a CTA range boundary; one CTA per
+// (sequence, kv head), one thread per (query head of the group, output element). Runs of an
+// empty sequence get a zero output; runs finished by one CTA are left as written.
+template <typename T, int D, int G>
+__global__ void decode_tma_merge_kernel(const DecArgs a, int grid) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x / a.n_heads_kv, hk = blockIdx.x % a.n_heads_kv;
+  const int g = threadIdx.x / D, e = threadIdx.x % D;
+  const int64_t total = a.ws_pre[a.batch];
+  const int tiles = (a.ws_pre[b + 1] - a.ws_pre[b]) / a.n_heads_kv;
+  const int64_t h = (int64_t)b * a.n_heads + hk * G + g;
+  if (tiles == 0) {
+    reinterpret_cast<T*>(a.out)[h * D + e] = DT<T>::from_f(0.f);
+    return;
+  }
+  const int64_t seg0 = a.ws_pre[b] + (int64_t)hk * tiles, seg1 = seg0 + tiles;
+  const int c0 = cta_of(seg0, total, grid), c1 = cta_of(seg1 - 1, total, grid);
+  if (c0 == c1) return;
+  float M = -INFINITY;
+  for (int c = c0; c <= c1; ++c) {
+    const int64_t slot = c == c0 ? 2 * (int64_t)c + 1 : 2 * (int64_t)c;
+    M = fmaxf(M, a.ws_ml[(slot * G + g) * 2]);
+  }
+  float Ls = 0.f, A = 0.f;
+  for (int c = c0; c <= c1; ++c) {
+    const int64_t slot = c == c0 ? 2 * (int64_t)c + 1 : 2 * (int64_t)c;
+    const float mc = a.ws_ml[(slot * G + g) * 2];
+    if (mc == -INFINITY) continue;
+    const float sc = exp2f(mc - M);
+    Ls += a.ws_ml[(slot * G + g) * 2 + 1] * sc;
+    A += a.ws_o[(slot * G + g) * D + e] * sc;
+  }
+  reinterpret_cast<T*>(a.out)[h * D + e] = DT<T>::from_f(Ls > 0.f ? A / Ls : 0.f);
+}
+
 template <typename T, int D, int G>
 int launch(const CUtensorMap& map, const DecArgs& args, int grid, cudaStream_t stream) {
   using L = DLay<D>;
   const size_t smem = (size_t)L::kRing + 1024 +
                       sizeof(float) * (G * D + kConsumers * G * D + kConsumers * G * 2 + 2) +
-                      2 * L::kStages * sizeof(uint64_t) + 64;
+                      2 * L::kStages * sizeof(uint64_t) + sizeof(int) * (kMaxSeqs + 1) + 64;
   auto kern = decode_tma_kernel<T, D, G>;
   static bool attr[64] = {false};
   int dev = 0;
@@ -335,35 +434,58 @@ int launch(const CUtensorMap& map, const DecArgs& args, int grid, cudaStream_t s
     if (s) return s;
     attr[dev & 63] = true;
   }
-  kern<<<grid, kThreadsTma, smem, stream>>>(map, args);
+  int s = hx::cuda_status(launch_ex(kern, dim3(grid), dim3(kThreadsTma), smem, stream, 1, map, args),
+                          "decode_tma_kernel launch");
+  if (s) return s;
   HX_LAUNCH_CHECK("decode_tma_kernel");
+  s = hx::cuda_status(launch_ex(decode_tma_merge_kernel<T, D, G>,
+                                dim3((unsigned)(args.batch * args.n_heads_kv)), dim3(G * D), 0,
+                                stream, 1, args, grid),
+                      "decode_tma_merge_kernel launch");
+  if (s) return s;
+  HX_LAUNCH_CHECK("decode_tma_merge_kernel");
   return HX_OK;
 }
 
 }  // namespace
 
+// Workspace of the balanced path: partials of 2 slots per CTA (each for a whole query-head
+// group, bounded here by n_heads) plus the tile prefix.
+size_t decode_tma_workspace(int64_t batch, int64_t n_heads, int64_t head_dim) {
+  const int64_t slots = 2 * (int64_t)device_sm_count();
+  return (size_t)slots * n_heads * (head_dim + 2) * sizeof(float) + (size_t)(batch + 1) * sizeof(int) + 256;
+}
+
 // Returns HX_ERR_UNSUPPORTED (without launching) for shapes this kernel does not cover.
 int decode_attention_tma(const void* q, const void* cache, int64_t cbs, int64_t css,
                          const int32_t* seqlens, int64_t batch, int64_t n_heads,
-                         int64_t n_heads_kv, int64_t head_dim, int splits, int chunk,
-                         float scale, void* out, float* ws_o, float* ws_ml, int dtype,
-                         cudaStream_t stream) {
+                         int64_t n_heads_kv, int64_t head_dim, float scale, void* out, void* ws,
+                         size_t ws_bytes, int dtype, cudaStream_t stream) {
   const int64_t group = n_heads / n_heads_kv;
   if ((dtype != HX_BF16 && dtype != HX_F16) || (head_dim != 64 && head_dim != 128) || group > 2 ||
-      chunk % kTileKeys || css % 8 || cbs % css || (uintptr_t)cache % 16)
+      batch > kMaxSeqs || css % 8 || cbs % css || (uintptr_t)cache % 16)
     return HX_ERR_UNSUPPORTED;
-  CUtensorMap map;
   const int64_t max_seq = cbs / css;
+  const int64_t max_tiles = (max_seq + kTileKeys - 1) / kTileKeys;
+  if (batch * n_heads_kv * max_tiles > INT32_MAX / 2) return HX_ERR_UNSUPPORTED;
+  const size_t need = decode_tma_workspace(batch, n_heads, head_dim);
+  HX_REQUIRE(ws && ws_bytes >= need, "hx_decode_attention: workspace too small (%zu < %zu)",
+             ws_bytes, need);
+  HX_REQUIRE((uintptr_t)ws % 16 == 0, "hx_decode_attention: workspace must be 16-byte aligned");
+  CUtensorMap map;
   const uint64_t dims[4] = {(uint64_t)head_dim, (uint64_t)(2 * n_heads_kv), (uint64_t)max_seq,
                             (uint64_t)batch};
   const uint64_t strides[3] = {(uint64_t)head_dim * 2, (uint64_t)css * 2, (uint64_t)cbs * 2};
   const uint32_t box[4] = {64, 1, (uint32_t)kTileKeys, 1};
   int s = make_tensor_map(&map, cache, 4, dims, strides, box, dtype);
   if (s) return s;
-  DecArgs args{q, out, ws_o, ws_ml, seqlens, (int)n_heads, (int)n_heads_kv, (int)batch, splits,
-               chunk, scale * 1.4426950408889634f};
-  const int64_t items = batch * n_heads_kv * splits;
-  const int grid = (int)std::min<int64_t>(items, device_sm_count());
+  const int grid = device_sm_count();
+  const int64_t slots = 2 * (int64_t)grid;
+  float* ws_o = (float*)ws;
+  float* ws_ml = ws_o + slots * group * head_dim;
+  int* ws_pre = (int*)(ws_ml + slots * group * 2);
+  DecArgs args{q, out, ws_o, ws_ml, ws_pre, seqlens, (int)n_heads, (int)n_heads_kv, (int)batch,
+               (int)max_seq, scale * 1.4426950408889634f};
 #define HX_DEC_TMA(TT, DD, GG) return launch<TT, DD, GG>(map, args, grid, stream)
   if (dtype == HX_BF16) {
     if (head_dim == 128) { if (group == 1) HX_DEC_TMA(__nv_bfloat16, 128, 1); HX_DEC_TMA(__nv_bfloat16, 128, 2); }

@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <type_traits>
+#include <utility>
 
 #include "../../include/hexgen2_b200.h"
 
@@ -310,6 +311,43 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_mn_maj
   uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn_major << 15) |
          ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Kernels launched with launch_ex() may start while the
+// previous kernel on the stream is still running: every thread calls pdl_wait() before it
+// reads or writes memory that an earlier kernel produces or consumes (it returns once all
+// prerequisite grids have completed and their memory is visible; without PDL it returns at
+// once). pdl_trigger() lets the next kernel be scheduled as soon as every CTA of this grid
+// has issued it, so its prologue overlaps this kernel's tail.
+// ---------------------------------------------------------------------------------------
+HX_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+HX_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: cudaLaunchKernelEx with programmatic stream serialization and an optional 1-D cluster.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, int cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------------------

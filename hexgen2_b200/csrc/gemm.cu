@@ -9,8 +9,10 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows), applies the epilogue, stores to global memory.
 //   The accumulator of tile i+1 is computed while tile i is being stored.
-// Decode-shaped problems (few tiles) split K across CTAs; partial sums go to a caller-provided
-// f32 workspace and a small kernel reduces them in split order and applies the epilogue.
+// Problems with M > 64 and too few tiles split K across CTAs; partial sums go to a
+// caller-provided f32 workspace and a small kernel reduces them in split order.
+// Decode-shaped problems (M <= 64) use gemm_decode_kernel: operands swapped and K split across
+// the CTAs of a thread-block cluster, reduced through distributed shared memory (no workspace).
 // f32: a CUDA-core tiled kernel with exact f32 products (the reference's f32 path).
 //
 // Epilogues reproduce the reference's rounding points:
@@ -26,14 +28,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 2 bytes = one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
 
-// kSwap: decode-shaped problems (M = batch <= 64) run with the operands swapped: the MMA's
-// 128-row side walks the weight rows (output features) and its N side is the batch, so no
-// tensor-core work or shared-memory bandwidth is spent on padding rows. Those configurations
-// use small rings (<= ~110 KB) so two CTAs fit on an SM.
-template <int BN, bool kSwap = false>
+template <int BN>
 struct Cfg {
-  static constexpr int kStages = kSwap ? (BN <= 16 ? 6 : (BN <= 32 ? 5 : 4))
-                                       : (BN == 256 ? 4 : (BN == 128 ? 6 : 8));
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -52,10 +49,6 @@ struct QkvArgs {
   int n_heads, n_heads_kv, head_dim, seqlen;
 };
 
-// Workspace layout (f16/bf16): [0, 64 KiB) per-tile arrival counters of the stream-K fixup
-// (zero between calls), then the f32 partial sums.
-constexpr size_t kFlagBytes = 64 * 1024;
-
 struct GemmArgs {
   int M, N, K;
   int m_tiles, n_tiles, k_splits, kb_per_split, k_blocks;
@@ -63,9 +56,7 @@ struct GemmArgs {
   int64_t ldc;
   const void* R;
   int64_t ldr;
-  float* ws;        // split-K partials [k_splits][M][N]; stream-K partials [ctas][segs][M][128]
-  uint32_t* flags;  // stream-K per-tile arrival counters
-  int ctas, segs;   // stream-K: CTAs sharing the units, max tile segments per CTA
+  float* ws;        // split-K partials [k_splits][M][N] (M > 64 only)
   QkvArgs qkv;
 };
 
@@ -366,100 +357,200 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------
-// Decode-shaped GEMM (M = batch <= 64): operands swapped + stream-K.
-//   MMA A = weight rows (128 per tile, K-major), MMA B = the batch rows (N = 16/32/64), so no
-//   tensor-core work or shared-memory bandwidth goes to padding rows. The (tile, k-block) units
-//   of the whole problem are divided evenly between ~2 CTAs per SM: every CTA streams the same
-//   number of weight bytes, with no wave tail. A CTA's range may start or end inside a tile; each
-//   tile part ("segment") is written as f32 to partial slot (cta, segment), and
-//   streamk_reduce_kernel sums the parts of each tile in CTA order and applies the epilogue.
+// Decode-shaped GEMM (M = batch <= 64): operands swapped, split-K inside a thread-block cluster.
+//   MMA A = 128 weight rows (output features) per tile, K-major; MMA B = the batch rows
+//   (N = 16/32/64, rows past M zero-filled by TMA), so no tensor-core work or shared-memory
+//   bandwidth goes to padding rows. The K range of a tile is split across the S CTAs of one
+//   cluster (S <= 8, chosen so that tiles x S fill ~2 CTAs per SM). Each CTA streams its slice
+//   of the weight tile through a TMA ring into one TMEM accumulator, writes the f32 partial
+//   [BN][128] into its own (now idle) ring, and after a cluster barrier CTA s sums batch rows
+//   b = s, s + S, ... of all S partials through distributed shared memory, in rank order
+//   (deterministic), and applies the epilogue. No global scratch, atomics or fences.
 // ------------------------------------------------------------------------------------------
-HX_DEVICE int64_t sk_unit_begin(int c, int64_t units, int ctas) { return (int64_t)c * units / ctas; }
+constexpr int kDecMaxStages = 16;
 
-// One output element of the swapped layout (feature n, batch row b), called by all 32 lanes
-// of a warp with a warp-uniform b (the epilogues exchange partners with shuffles).
+HX_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+HX_DEVICE uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+HX_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// Address of the same shared variable in CTA `rank` of this cluster.
+HX_DEVICE uint32_t dsmem_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+HX_DEVICE float dsmem_ld_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+// Eight output rows at once (batch rows b[0..nr), one feature n per lane, warp-uniform rows):
+// every global load the epilogue needs (residual, rotary tables) is issued for all rows before
+// any result is computed or stored, so a group costs one memory round trip instead of eight.
+// pos_s[m] = position of batch row m (fused Wqkv epilogue only), preloaded in shared memory.
 template <typename T, int EPI>
-HX_DEVICE void sk_store(const GemmArgs& a, int b, int n, int lane, float v) {
+HX_DEVICE void sk_store8(const GemmArgs& a, const int (&b)[8], int nr, int n, int lane,
+                         const float (&v)[8], const int* pos_s) {
   if (EPI == HX_EPI_SWIGLU) {
-    // Rows [32k, 32k+16) of a tile are up, [32k+16, 32k+32) the matching gates.
-    const float gate = __shfl_xor_sync(0xffffffffu, v, 16);
-    if (lane < 16 && b < a.M && n < a.N) {
-      const float u = round_to<T>(v), g = round_to<T>(gate);
-      reinterpret_cast<T*>(a.C)[(int64_t)b * a.ldc + (n >> 5) * 16 + lane] =
-          DT<T>::from_f(u * round_to<T>(silu_f(g)));
+    float gate[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gate[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
+    if (lane < 16 && n < a.N) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < nr && b[i] < a.M) {
+          const float u = round_to<T>(v[i]), g = round_to<T>(gate[i]);
+          reinterpret_cast<T*>(a.C)[(int64_t)b[i] * a.ldc + (n >> 5) * 16 + lane] =
+              DT<T>::from_f(u * round_to<T>(silu_f(g)));
+        }
+      }
     }
   } else if (EPI == HX_EPI_QKV_ROTARY) {
-    const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-    if ((lane & 1) == 0) qkv_store_pair<T>(a, b, n, v, other);
-  } else if (b < a.M && n < a.N) {
-    float x = round_to<T>(v);
-    if (EPI == HX_EPI_RESIDUAL)
-      x += DT<T>::to_f(reinterpret_cast<const T*>(a.R)[(int64_t)b * a.ldr + n]);
-    reinterpret_cast<T*>(a.C)[(int64_t)b * a.ldc + n] = DT<T>::from_f(x);
+    float other[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
+    if ((lane & 1) || n >= a.N) return;
+    const QkvArgs& q = a.qkv;
+    const int hqd = q.n_heads * q.head_dim;
+    const bool rot = n < hqd + q.n_heads_kv * q.head_dim;
+    const int pair = (n % q.head_dim) >> 1;
+    const T* cos_t = reinterpret_cast<const T*>(q.cos);
+    const T* sin_t = reinterpret_cast<const T*>(q.sin);
+    int64_t pos[8];
+    T cv[8], sv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pos[i] = -1;
+      if (i < nr && b[i] < a.M) {
+        pos[i] = pos_s[b[i]];
+        if (rot && pos[i] >= 0 && pos[i] < q.table_rows) {
+          cv[i] = __ldg(cos_t + pos[i] * (q.head_dim / 2) + pair);
+          sv[i] = __ldg(sin_t + pos[i] * (q.head_dim / 2) + pair);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (!(i < nr && b[i] < a.M)) continue;
+      const int m = b[i];
+      if (pos[i] < 0 || pos[i] >= q.max_seq || pos[i] >= q.table_rows) {
+        record_device_error(HX_DEVERR_BAD_ARGUMENT);
+        continue;
+      }
+      float x0 = round_to<T>(v[i]), x1 = round_to<T>(other[i]);
+      if (rot) {
+        const float c = DT<T>::to_f(cv[i]), sn = DT<T>::to_f(sv[i]);
+        const float o0 = x0 * c - x1 * sn;
+        const float o1 = x0 * sn + x1 * c;
+        x0 = o0;
+        x1 = o1;
+      }
+      const int bb = m / q.seqlen;
+      T* dst = n < hqd ? reinterpret_cast<T*>(q.q_out) + (int64_t)m * hqd + n
+                       : reinterpret_cast<T*>(q.cache) + (q.cbo + bb) * q.cbs + pos[i] * q.css + (n - hqd);
+      T pr2[2] = {DT<T>::from_f(x0), DT<T>::from_f(x1)};
+      *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(pr2);
+    }
+  } else {
+    float r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      r[i] = 0.f;
+      if (EPI == HX_EPI_RESIDUAL && i < nr && b[i] < a.M && n < a.N)
+        r[i] = DT<T>::to_f(reinterpret_cast<const T*>(a.R)[(int64_t)b[i] * a.ldr + n]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < nr && b[i] < a.M && n < a.N) {
+        float x = round_to<T>(v[i]);
+        if (EPI == HX_EPI_RESIDUAL) x += r[i];
+        reinterpret_cast<T*>(a.C)[(int64_t)b[i] * a.ldc + n] = DT<T>::from_f(x);
+      }
+    }
   }
 }
 
 template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 2)
-    gemm_streamk_kernel(const __grid_constant__ CUtensorMap tmW,
-                        const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
-  using C = Cfg<BN, true>;
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW,
+                       const __grid_constant__ CUtensorMap tmX, const GemmArgs a, int stages) {
+  constexpr int kWBytes = BM * BK * 2;
+  constexpr int kXBytes = BN * BK * 2;
+  constexpr int kStageBytes = kWBytes + kXBytes;
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smA = smem;
-  uint8_t* smB = smem + C::kStages * C::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smB + C::kStages * C::kBBytes);
-  uint64_t* empty = full + C::kStages;
-  uint64_t* tfull = empty + C::kStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint32_t* counters = reinterpret_cast<uint32_t*>(drain + 1);
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * kStageBytes);
+  uint64_t* empty = full + kDecMaxStages;
+  uint64_t* tfull = empty + kDecMaxStages;
+  uint32_t* counters = reinterpret_cast<uint32_t*>(tfull + 1);  // [0] loads issued, [1] consumed
   uint32_t* tmem_slot = counters + 2;
-  volatile uint32_t* sk_last = tmem_slot + 1;                          // fixup decision
-  int64_t* sk_off = reinterpret_cast<int64_t*>(tmem_slot + 2);        // [<= 24] part offsets
+  int* pos_s = reinterpret_cast<int*>(counters + 4);             // [BN] row positions (Wqkv)
+  float* part = reinterpret_cast<float*>(ring);                  // [BN][BM] f32 after the loop
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kb = a.k_blocks;
-  const int64_t units = (int64_t)a.m_tiles * kb;
-  const int64_t u0 = sk_unit_begin(blockIdx.x, units, gridDim.x);
-  const int64_t u1 = sk_unit_begin(blockIdx.x + 1, units, gridDim.x);
+  const int S = a.k_splits;
+  const int split = S > 1 ? (int)cluster_ctarank() : 0;
+  const int tile = S > 1 ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int kb0 = split * a.kb_per_split;
+  const int kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmW);
     prefetch_tensormap(&tmX);
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
-    }
-    mbar_init(drain, 1);
+    mbar_init(tfull, 1);
     counters[0] = counters[1] = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (!(warp == 0 && lane == 0)) pdl_wait();  // the producer waits after its weight prefetch
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, issued = 0;
-      for (int64_t u = u0; u < u1; ++u) {
-        const int t = (int)(u / kb), kbi = (int)(u - (int64_t)t * kb);
+      // The weights are not produced by earlier kernels: the first ring's worth of weight
+      // tiles is requested before waiting for the previous kernel (PDL), so the stream of
+      // weight bytes starts while that kernel drains. Activation tiles follow the wait.
+      const int pre = min(stages, kb1 - kb0);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], kStageBytes);
+        tma_load_2d(ring + i * kStageBytes, &tmW, &full[i], (kb0 + i) * BK, tile * BM);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(ring + i * kStageBytes + kWBytes, &tmX, &full[i], (kb0 + i) * BK, 0);
+      int stage = pre == stages ? 0 : pre;
+      uint32_t phase = pre == stages ? 1 : 0, issued = pre;
+      for (int kb = kb0 + pre; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1)) break;
-        mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-        tma_load_2d(smA + stage * C::kABytes, &tmW, &full[stage], kbi * BK, t * BM);
-        tma_load_2d(smB + stage * C::kBBytes, &tmX, &full[stage], kbi * BK, 0);
+        mbar_arrive_expect_tx(&full[stage], kStageBytes);
+        uint8_t* st = ring + stage * kStageBytes;
+        tma_load_2d(st, &tmW, &full[stage], kb * BK, tile * BM);
+        tma_load_2d(st + kWBytes, &tmX, &full[stage], kb * BK, 0);
         ++issued;
-        if (++stage == C::kStages) {
+        if (++stage == stages) {
           stage = 0;
           phase ^= 1;
         }
@@ -469,134 +560,123 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16<T>(BM, BN);
-      int stage = 0, seg = -1, cur = -1, acc = 0;
+      int stage = 0;
       uint32_t phase = 0, consumed = 0;
-      bool first = false;
-      for (int64_t u = u0; u < u1; ++u) {
-        const int t = (int)(u / kb);
-        if (t != cur) {  // a new tile segment starts: take the next accumulator buffer
-          if (cur >= 0) tc_commit(&tfull[acc]);
-          ++seg;
-          acc = seg & 1;
-          if (!mbar_wait(&tempty[acc], ((seg >> 1) & 1) ^ 1)) goto sk_mma_done;
-          tc_fence_after();
-          cur = t;
-          first = true;
-        }
-        if (!mbar_wait(&full[stage], phase)) goto sk_mma_done;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase)) break;
         ++consumed;
         tc_fence_after();
-        {
-          const uint32_t a_addr = smem_u32(smA + stage * C::kABytes);
-          const uint32_t b_addr = smem_u32(smB + stage * C::kBBytes);
+        const uint32_t a_addr = smem_u32(ring + stage * kStageBytes);
+        const uint32_t b_addr = a_addr + kWBytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            tc_mma_f16(tmem_base + acc * BN, sw128_kmajor_desc(a_addr + k * 32),
-                       sw128_kmajor_desc(b_addr + k * 32), idesc, (first && k == 0) ? 0u : 1u);
-        }
-        first = false;
+        for (int k = 0; k < BK / 16; ++k)
+          tc_mma_f16(tmem_base, sw128_kmajor_desc(a_addr + k * 32),
+                     sw128_kmajor_desc(b_addr + k * 32), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
         tc_commit(&empty[stage]);
-        if (++stage == C::kStages) {
+        if (++stage == stages) {
           stage = 0;
           phase ^= 1;
         }
       }
-      if (cur >= 0) tc_commit(&tfull[acc]);
-    sk_mma_done:
-      tc_commit(drain);
-      mbar_wait(drain, 0);
+      // Completes once every MMA above has finished (also with none issued). After a timed-out
+      // wait the accumulator is incomplete; the device error word already says so.
+      tc_commit(tfull);
       counters[1] = consumed;
     }
-  } else if (u1 > u0) {
-    // Epilogue warps 2..5 (named barrier 2). A tile this CTA owns alone is stored straight from
-    // TMEM. Otherwise the part goes to partial slot (cta, segment); the CTA that completes a
-    // tile's arrival count sums all parts of the tile in CTA order (deterministic), applies the
-    // epilogue, and resets the counter for the next call.
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4 = tile rows 32q..32q+31.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int t_first = (int)(u0 / kb), t_last = (int)((u1 - 1) / kb);
-    for (int t = t_first, seg = 0; t <= t_last; ++t, ++seg) {
-      const int acc = seg & 1;
-      if (!named_bar_and(2, 128, mbar_wait_warp(&tfull[acc], (seg >> 1) & 1))) break;
-      tc_fence_after();
-      const int64_t ua = (int64_t)t * kb, ub = (int64_t)(t + 1) * kb - 1;
-      const int c0 = (int)(((ua + 1) * a.ctas - 1) / units);
-      const int c1 = (int)(((ub + 1) * a.ctas - 1) / units);
-      const int n = t * BM + r;
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      if (c0 == c1) {
+    if (EPI == HX_EPI_QKV_ROTARY) {
+      // Row positions, loaded while the main loop runs.
+      const QkvArgs& q = a.qkv;
+      for (int m = threadIdx.x - 64; m < min(BN, a.M); m += 128)
+        pos_s[m] = q.pos_start[m / q.seqlen] + m % q.seqlen;
+      named_bar_sync(2, 128);
+    }
+    const bool ready = mbar_wait_warp(tfull, 0);
+    tc_fence_after();
+    const bool valid = ready && kb1 > kb0;
+    const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    if (S == 1) {
+      if (valid) {
 #pragma unroll
         for (int c = 0; c < BN / 16; ++c) {
           uint32_t v[16];
           tmem_ld_32x32b_x16(taddr + c * 16, v);
           tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) sk_store<T, EPI>(a, c * 16 + j, n, lane, __uint_as_float(v[j]));
+          for (int h = 0; h < 2; ++h) {
+            int rows[8];
+            float vals[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              rows[j] = c * 16 + h * 8 + j;
+              vals[j] = __uint_as_float(v[h * 8 + j]);
+            }
+            sk_store8<T, EPI>(a, rows, 8, tile * BM + r, lane, vals, pos_s);
+          }
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
-        continue;
       }
-      float* slot = a.ws + ((int64_t)blockIdx.x * a.segs + seg) * a.M * BM;
+    } else {
+      // The ring is idle once every MMA has completed (all issued loads were consumed).
 #pragma unroll
       for (int c = 0; c < BN / 16; ++c) {
         uint32_t v[16];
-        tmem_ld_32x32b_x16(taddr + c * 16, v);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int b = c * 16 + j;
-          if (b < a.M) slot[(int64_t)b * BM + r] = __uint_as_float(v[j]);
+        if (valid) {
+          tmem_ld_32x32b_x16(taddr + c * 16, v);
+          tc_wait_ld();
         }
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
-      __threadfence();
-      named_bar_sync(2, 128);
-      const int parts = c1 - c0 + 1;
-      if (threadIdx.x == 64) {
-        const uint32_t old = atomicAdd(&a.flags[t], 1u);
-        *sk_last = (old == (uint32_t)(parts - 1)) ? 1u : 0u;
-      }
-      if (r < parts && r < 24) {  // offsets of the parts, contributor order
-        const int c = c0 + r;
-        const int seg_c = t - (int)(((int64_t)c * units / a.ctas) / kb);
-        sk_off[r] = ((int64_t)c * a.segs + seg_c) * a.M * BM;
-      }
-      named_bar_sync(2, 128);
-      if (*sk_last) {
-        __threadfence();
-        if (parts > 24) {
-          if (r == 0) record_device_error(HX_DEVERR_BAD_ARGUMENT);
-        } else {
-          // All rows' loads are issued before any store, so the L2 round trips overlap.
-          float sum[BN];
 #pragma unroll
-          for (int b = 0; b < BN; ++b) sum[b] = 0.f;
-          for (int i = 0; i < parts; ++i) {
-            const float* src = a.ws + sk_off[i] + r;
-#pragma unroll
-            for (int b = 0; b < BN; ++b)
-              if (b < a.M) sum[b] += src[(int64_t)b * BM];
-          }
-#pragma unroll
-          for (int b = 0; b < BN; ++b) sk_store<T, EPI>(a, b, n, lane, sum[b]);
-        }
-        if (threadIdx.x == 64) a.flags[t] = 0u;
+        for (int j = 0; j < 16; ++j) part[(c * 16 + j) * BM + r] = valid ? __uint_as_float(v[j]) : 0.f;
       }
-      named_bar_sync(2, 128);
     }
+  }
+
+  if (S > 1) {
+    __syncwarp();
+    cluster_sync_all();  // every partial of the cluster is in shared memory
+    if (warp >= 2) {
+      // CTA `split` owns batch rows split, split + S, ...; eight at a time, all S x 8 partial
+      // loads in flight together, summed in rank order.
+      const int r = (warp & 3) * 32 + lane;
+      const int rows = min(BN, a.M);
+      const uint32_t my = smem_u32(part + r);
+      for (int b0 = split; b0 < rows; b0 += 8 * S) {
+        int bs[8];
+        float sums[8];
+        const int nr = min(8, (rows - b0 + S - 1) / S);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          bs[i] = b0 + i * S;
+          float v[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            v[c] = (c < S && i < nr) ? dsmem_ld_f32(dsmem_map(my + (uint32_t)(bs[i] * BM * 4), (uint32_t)c)) : 0.f;
+          float sum = 0.f;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c < S) sum += v[c];
+          sums[i] = sum;
+        }
+        sk_store8<T, EPI>(a, bs, nr, tile * BM + r, lane, sums, pos_s);
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while another still reads its partial
   }
 
   tc_fence_before();
   __syncthreads();
+  // After an aborted wait, loads may have been issued that nobody consumed: let them land
+  // (bounded) before the CTA's shared memory goes away.
   if (threadIdx.x == 0) {
     for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1)) break;
+      if (!mbar_wait(&full[i % stages], (i / stages) & 1)) break;
   }
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
 }
 
 // Split-K reduction in split order + epilogue. One thread per output element.
@@ -713,35 +793,24 @@ int device_sms() { return device_sm_count(); }
 
 struct Plan {
   int bn, m_tiles, n_tiles, k_splits, kb_per_split, k_blocks;
-  bool swap;        // decode-shaped: operands swapped, stream-K
-  int ctas, segs;   // stream-K CTAs and max tile segments per CTA
+  bool swap;    // decode-shaped: operands swapped, split-K inside a cluster (chosen at launch)
 };
 
 // Tile / split selection.
 //  * Decode-shaped (M <= 64): operands swapped (128 weight rows per tile, N = batch rounded up
-//    to 16/32/64) and stream-K over ~2 CTAs per SM.
+//    to 16/32/64); the K split across a cluster is chosen by launch_decode.
 //  * Otherwise: the widest tile that still fills the machine; split K if there are too few
-//    tiles for the SMs.
+//    tiles for the SMs (partials reduced by a second kernel in split order).
 Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
   const int sms = device_sms();
   Plan p;
   p.k_blocks = ceil_div(K, BK);
   p.swap = M <= 64;
-  p.ctas = p.segs = 0;
   int splits = 1;
   if (p.swap) {
     p.bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     p.m_tiles = ceil_div(N, BM);
     p.n_tiles = 1;
-    const int64_t units = (int64_t)p.m_tiles * p.k_blocks;
-    p.ctas = (int)std::min<int64_t>(units, 2 * (int64_t)sms);
-    if ((units + 1) * (int64_t)p.ctas > INT32_MAX) p.swap = false;  // reduce uses 32-bit math
-    int segs = 1;
-    for (int c = 0; c < p.ctas; ++c) {
-      const int64_t u0 = (int64_t)c * units / p.ctas, u1 = (int64_t)(c + 1) * units / p.ctas;
-      segs = std::max(segs, (int)((u1 - 1) / p.k_blocks - u0 / p.k_blocks + 1));
-    }
-    p.segs = segs;
   } else {
     p.m_tiles = ceil_div(M, BM);
     const int64_t t256 = (int64_t)p.m_tiles * ceil_div(N, 256);
@@ -757,32 +826,56 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
     }
   }
   p.kb_per_split = ceil_div(p.k_blocks, splits);
-  p.k_splits = ceil_div(p.k_blocks, p.kb_per_split);
+  p.k_splits = ceil_div(p.k_blocks, p.kb_per_split);  // every split non-empty
   return p;
 }
 
 size_t plan_workspace(const Plan& p, int64_t M, int64_t N) {
-  if (p.swap) return kFlagBytes + (size_t)p.ctas * p.segs * M * BM * sizeof(float);
-  return p.k_splits > 1 ? kFlagBytes + (size_t)p.k_splits * M * N * sizeof(float) : 0;
+  if (p.swap) return 0;
+  return p.k_splits > 1 ? (size_t)p.k_splits * M * N * sizeof(float) : 0;
 }
 
+// Decode GEMM launch. The K split S (= cluster size) is the largest S <= 8 with
+// tiles x S <= 1.6 x SMs and at least two k-blocks per split: enough CTAs to keep every SM
+// streaming weights, few enough that the clusters are co-resident (measured on B200: 3-CTA
+// clusters x 96 tiles = 288 CTAs ran ~40% slower than 2 x 96, and 8 x 32 tiles was the best
+// split for 32-tile shapes). The ring takes ~200 KB per CTA when the CTAs do not outnumber
+// the SMs, ~100 KB when two share an SM.
 template <typename T, int BN, int EPI>
-int launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& a,
-                   cudaStream_t stream) {
-  using C = Cfg<BN, true>;
-  auto kern = gemm_streamk_kernel<T, BN, EPI>;
+int launch_decode(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& a0,
+                  cudaStream_t stream) {
+  auto kern = gemm_decode_kernel<T, BN, EPI>;
+  constexpr int stage_bytes = BM * BK * 2 + BN * BK * 2;
+  constexpr size_t smem_fixed = 1024 + 2 * kDecMaxStages * 8 + 64 + 64 * sizeof(int);
+  const size_t smem_max = smem_fixed + (size_t)kDecMaxStages * stage_bytes;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
     int s = hx::cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)C::kSmemBytes),
-                            "cudaFuncSetAttribute(gemm_streamk)");
+                                                 (int)std::min<size_t>(smem_max, 227 * 1024)),
+                            "cudaFuncSetAttribute(gemm_decode)");
     if (s) return s;
     attr_set[dev & 63] = true;
   }
-  kern<<<a.ctas, kGemmThreads, C::kSmemBytes, stream>>>(mw, mx, a);
-  HX_LAUNCH_CHECK("gemm_streamk_kernel");
+  const int sms = device_sms();
+  GemmArgs a = a0;
+  const int64_t max_ctas = (int64_t)sms * 8 / 5;
+  int split = (int)std::max<int64_t>(1, std::min<int64_t>({8, max_ctas / a.m_tiles, a.k_blocks / 2}));
+  split = ceil_div(a.k_blocks, ceil_div(a.k_blocks, split));  // every split owns k-blocks
+  const int kbs = ceil_div(a.k_blocks, split);
+  const int64_t ctas = (int64_t)a.m_tiles * split;
+  const int budget = ctas <= sms ? 200 * 1024 : 100 * 1024;
+  const int stages = std::min(std::max(2, std::min(kDecMaxStages, budget / stage_bytes)),
+                              std::max(2, kbs));
+  a.k_splits = split;
+  a.kb_per_split = ceil_div(a.k_blocks, split);
+  const size_t smem = smem_fixed + (size_t)stages * stage_bytes;
+  int s = hx::cuda_status(launch_ex(kern, dim3((unsigned)(a.m_tiles * split)), dim3(kGemmThreads),
+                                    smem, stream, split, mw, mx, a, stages),
+                          "gemm_decode_kernel launch");
+  if (s) return s;
+  HX_LAUNCH_CHECK("gemm_decode_kernel");
   return HX_OK;
 }
 
@@ -827,18 +920,12 @@ int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int6
   a.R = R;
   a.ldr = ldr;
   a.ws = nullptr;
-  a.flags = nullptr;
-  a.ctas = p.ctas;
-  a.segs = p.segs;
   if (qkv) a.qkv = *qkv;
   const size_t need = plan_workspace(p, M, N);
   if (need) {
     HX_REQUIRE(ws && ws_bytes >= need, "hx_gemm: workspace too small (%zu < %zu)", ws_bytes, need);
     HX_REQUIRE((uintptr_t)ws % 16 == 0, "hx_gemm: workspace must be 16-byte aligned");
-    a.flags = (uint32_t*)ws;
-    a.ws = (float*)((uint8_t*)ws + kFlagBytes);
-    HX_REQUIRE(!p.swap || p.m_tiles <= (int)(kFlagBytes / sizeof(uint32_t)),
-               "hx_gemm: n too large for the tile counters");
+    a.ws = (float*)ws;
   }
   CUtensorMap ma, mb;
   int s;
@@ -849,9 +936,9 @@ int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int6
     s = make_map(&mb, A, M, K, lda, p.bn, dtype);
     if (s) return s;
     switch (p.bn) {
-      case 16: return launch_streamk<T, 16, EPI>(ma, mb, a, stream);
-      case 32: return launch_streamk<T, 32, EPI>(ma, mb, a, stream);
-      default: return launch_streamk<T, 64, EPI>(ma, mb, a, stream);
+      case 16: return launch_decode<T, 16, EPI>(ma, mb, a, stream);
+      case 32: return launch_decode<T, 32, EPI>(ma, mb, a, stream);
+      default: return launch_decode<T, 64, EPI>(ma, mb, a, stream);
     }
   } else {
     s = make_map(&ma, A, M, K, lda, BM, dtype);

@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     int64_t hidden, int64_t in_stride, int64_t out_stride, float eps) {
   extern __shared__ float smem_row[];  // hidden floats: the residual row in f32
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const T* xr = ids ? x + ids[row] * hidden : x + row * in_stride;
   const T* ar = add ? add + row * in_stride : nullptr;
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(
     T* __restrict__ out, const T* __restrict__ weight, const int64_t* __restrict__ ids,
     int64_t hidden, int64_t in_stride, int64_t out_stride, float eps) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const int t = threadIdx.x;
   const int64_t off = (int64_t)t * 8;
@@ -161,9 +165,12 @@ int launch_rmsnorm(const void* x, const void* add, void* residual_out, void* out
                    (!residual_out || (uintptr_t)residual_out % 16 == 0);
   if constexpr (sizeof(T) == 2) {
     if (vec && hidden % 256 == 0 && hidden <= 8192) {
-      rmsnorm_vec_kernel<T><<<(unsigned)rows, (unsigned)(hidden / 8), 0, stream>>>(
-          (const T*)x, (const T*)add, (T*)residual_out, (T*)out, (const T*)weight, ids, hidden,
-          in_stride, out_stride, eps);
+      const int s = hx::cuda_status(
+          launch_ex(rmsnorm_vec_kernel<T>, dim3((unsigned)rows), dim3((unsigned)(hidden / 8)), 0,
+                    stream, 1, (const T*)x, (const T*)add, (T*)residual_out, (T*)out,
+                    (const T*)weight, ids, hidden, in_stride, out_stride, eps),
+          "rmsnorm_vec_kernel launch");
+      if (s) return s;
       HX_LAUNCH_CHECK("rmsnorm_vec_kernel");
       return HX_OK;
     }
@@ -173,9 +180,12 @@ int launch_rmsnorm(const void* x, const void* add, void* residual_out, void* out
   auto kern = vec ? rmsnorm_kernel<T, true> : rmsnorm_kernel<T, false>;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<(unsigned)rows, kNormThreads, smem, stream>>>(
-      (const T*)x, (const T*)add, (T*)residual_out, (T*)out, (const T*)weight, ids, hidden,
-      in_stride, out_stride, eps);
+  const int s = hx::cuda_status(
+      launch_ex(kern, dim3((unsigned)rows), dim3(kNormThreads), smem, stream, 1, (const T*)x,
+                (const T*)add, (T*)residual_out, (T*)out, (const T*)weight, ids, hidden,
+                in_stride, out_stride, eps),
+      "rmsnorm_kernel launch");
+  if (s) return s;
   HX_LAUNCH_CHECK("rmsnorm_kernel");
   return HX_OK;
 }

@@ -201,18 +201,34 @@ class Engine:
         (lengths: int32 device [B], advanced in place). Returns tokens [B, steps + 1] on the
         device (column 0 = first_tokens).
 
-        With use_graph, the first step runs eagerly (it also sizes every scratch buffer) and one
-        single-token step is captured in a CUDA graph that is replayed for the rest: its input
-        is the static token buffer the previous replay's argmax wrote, and the length increment
-        is part of the graph, so a replay is one launch from the host."""
+        With use_graph, one single-token step is captured in a CUDA graph whose input is a
+        static token buffer that the previous replay's argmax wrote and whose length increment
+        is part of the graph, so a step is one launch from the host. The graph is kept per
+        (batch, cache, lengths, scratch buffers, rotary tables) and replayed by later calls on
+        the same buffers; the first call runs one step eagerly (it also sizes every scratch
+        buffer) and captures."""
         B = first_tokens.numel()
         capacity = caches[0].shape[1]
         tokens = torch.empty(steps + 1, B, dtype=torch.long, device=self.device)
         tokens[0] = first_tokens.reshape(B)
-        state = CacheState(capacity, max_batch_size=B)
-        state.key_value_memory_dict = caches
-        state.lengths_per_sample = lengths
-        cur = torch.empty(B, 1, dtype=torch.long, device=self.device)
+        if steps <= 0:
+            return tokens.t()
+        profiling = ops.PROFILE is not None
+
+        def graph_key():
+            cos = self.model.rope_tables(capacity, self.device, self.dtype)[0]
+            return (B, capacity, caches[0].data_ptr(), lengths.data_ptr(), ops.WORKSPACE_GEN,
+                    cos.data_ptr())
+
+        graphs = self.__dict__.setdefault("_decode_graphs", {})
+        entry = None if (profiling or not use_graph) else graphs.get(graph_key())
+        if entry is None:
+            state = CacheState(capacity, max_batch_size=B)
+            state.key_value_memory_dict = caches
+            state.lengths_per_sample = lengths
+            cur = torch.empty(B, 1, dtype=torch.long, device=self.device)
+        else:
+            graph, cur, per_replay = entry
         cur.copy_(tokens[0].view(B, 1))
 
         def step():
@@ -220,33 +236,41 @@ class Engine:
             lengths.add_(1)
             ops.argmax(logits, out=cur.view(B))
 
-        graph = None
-        per_replay = 0
         captured = []  # per-kernel event pairs recorded as graph nodes (profiling only)
         for s in range(steps):
-            if graph is not None:
+            if entry is not None:
                 graph.replay()
                 ops.LAUNCHES += per_replay  # kernels of this library inside one replay
-            elif use_graph and s >= 1 and steps - s > 1:
+            elif use_graph and s >= 1 and (steps - s > 1 or not profiling):
                 graph = torch.cuda.CUDAGraph()
                 before = ops.LAUNCHES
-                mark = len(ops.PROFILE) if ops.PROFILE is not None else 0
+                mark = len(ops.PROFILE) if profiling else 0
                 with torch.cuda.graph(graph):
                     step()
                 per_replay = ops.LAUNCHES - before  # counted once at capture = first replay
-                if ops.PROFILE is not None:
+                if profiling:
                     captured = ops.PROFILE[mark:]
                     del ops.PROFILE[mark:]
+                entry = (graph, cur, per_replay)
+                if not profiling:
+                    if len(graphs) >= 4:
+                        graphs.pop(next(iter(graphs)))
+                    graphs[graph_key()] = entry
                 graph.replay()
             else:
                 step()
-            if captured and graph is not None:
+            if captured:
                 # Profiling: read this replay's kernel timestamps before the next replay
                 # overwrites them.
                 torch.cuda.synchronize()
                 ops.PROFILE.extend(ops.profile_durations(captured))
             tokens[s + 1].copy_(cur.view(B))
         return tokens.t()
+
+    def release_graphs(self):
+        """Drops the kept decode graphs (needed before tearing down a process group whose
+        collectives they captured)."""
+        self.__dict__.pop("_decode_graphs", None)
 
     @torch.inference_mode()
     def serve_batch(self, prompts, lengths=None, max_new_tokens=16):

@@ -46,6 +46,9 @@ _workspaces: dict[int, torch.Tensor] = {}
 # launching stream.
 LAUNCHES = 0
 PROFILE: list | None = None
+# Bumped whenever a scratch buffer is reallocated: CUDA graphs that captured the old address
+# must not be replayed.
+WORKSPACE_GEN = 0
 
 
 def _begin(name):
@@ -76,19 +79,19 @@ def profile_durations(entries) -> list:
 
 
 def workspace(nbytes: int, device=None, kind: str = "attn") -> torch.Tensor | None:
-    """Per-device scratch buffer of at least nbytes (None for 0). kind="gemm" buffers start
-    zeroed: their first 64 KiB are the GEMM's tile counters, which every completed call leaves
-    at zero, so the buffer is reused as is."""
+    """Per-device scratch buffer of at least nbytes (None for 0), one per kind, reused across
+    calls on the same stream (GEMM split-K partials, decode-attention split partials)."""
     if nbytes == 0:
         return None
     dev = torch.cuda.current_device() if device is None else torch.device(device).index
     key = (dev, kind)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
+        global WORKSPACE_GEN
         size = max(nbytes, 0 if buf is None else buf.numel() * 2)
-        alloc = torch.zeros if kind == "gemm" else torch.empty
-        buf = alloc(size, dtype=torch.uint8, device=f"cuda:{dev}")
+        buf = torch.empty(size, dtype=torch.uint8, device=f"cuda:{dev}")
         _workspaces[key] = buf
+        WORKSPACE_GEN += 1
     return buf
 
 

@@ -103,16 +103,20 @@ int hx_rotary_cache_write(const void* qkv, int64_t batch, int64_t seqlen, int64_
  * For HX_EPI_SWIGLU, n counts interleaved B rows (2 * intermediate) and C has n/2 columns.
  * `workspace` may be NULL when hx_gemm_workspace() returns 0 for the shape; otherwise it must
  * hold that many bytes (split-K partial sums).
+ * Decode-shaped calls (m <= 64) use programmatic dependent launch and may start reading `b`
+ * (the weight) before the previous kernel on the stream has finished, when that kernel is one of
+ * this library's: `b` must not be written by the immediately preceding hx_* call on the stream
+ * (weights never are). Every other input and the output wait for the previous kernel.
  * Replaces nn.Linear (mha.py:395/:412, mlp.py:73-87, gpt.py:440) + the residual add of
  * block.py:155-158 + the SwiGLU of mlp.py:79-87. */
 int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
             int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
             int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
             void* stream);
-/* Workspace bytes for hx_gemm / hx_gemm_qkv_rotary. For f16/bf16 the first 64 KiB of a
- * workspace are per-tile arrival counters of the in-kernel split reduction: they must be zero
- * before the first call that uses the workspace and every completed call leaves them zero, so
- * allocate the workspace zeroed once and give each concurrently running stream its own. */
+/* Workspace bytes for hx_gemm / hx_gemm_qkv_rotary: f32 split-K partial sums, needed only
+ * when m > 64 and the output has too few tiles to fill the GPU (0 otherwise; decode-shaped
+ * problems, m <= 64, reduce their K splits inside a thread-block cluster and never need one).
+ * Calls that run concurrently need separate workspaces. */
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
 
 /* Wqkv projection fused with rotary and the KV-cache write: computes qkv = x * Wqkv^T

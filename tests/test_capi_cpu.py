@@ -39,7 +39,12 @@ def test_workspace_queries_need_no_gpu():
     from hexgen2_b200 import _lib
     lib = _lib.lib()
     assert lib.hx_gemm_workspace(1, 64, 64, 0, _lib.HX_F32) == 0
-    assert lib.hx_decode_attention_workspace(1, 32, 128, 16) == 0
+    # Decode-shaped bf16 GEMMs reduce inside a cluster: no workspace.
+    assert lib.hx_gemm_workspace(32, 4096, 4096, 0, _lib.HX_BF16) == 0
+    assert lib.hx_gemm_workspace(300, 512, 2048, 0, _lib.HX_BF16) > 0
+    # head_dim 32: one key split, no partials; head_dim 128: the balanced path's partials.
+    assert lib.hx_decode_attention_workspace(1, 32, 32, 16) == 0
+    assert lib.hx_decode_attention_workspace(1, 32, 128, 16) > 0
     assert lib.hx_decode_attention_workspace(1, 32, 128, 8192) > 0
 
 

@@ -202,3 +202,29 @@ def test_tp_rejects_bad_sizes(hx):
         class C:
             n_head, n_head_kv, n_embd, vocab_size, n_layer = 6, 6, 48, 10, 1
         shard_state_dict_tp({}, C, 4, 0)
+
+
+def test_decode_graph_is_kept_and_replayed(hx):
+    """A second decode_batch on the same buffers replays the kept CUDA graph (no recapture)
+    and produces the same tokens as the first call and as an eager run."""
+    oracle, eng = _oracle_and_engine(hx, dict(TINYLLAMA, vocab_size=4096), 2, torch.bfloat16, seed=6)
+    prompts = [list(range(7, 7 + L)) for L in (33, 5, 90)]
+    firsts, caches, lens = [], [], []
+    for p in prompts:
+        f, c, _ = eng.prefill(p, 16)
+        firsts.append(f)
+        caches.append(c)
+        lens.append(len(p))
+    steps = 12
+    full = eng.unpack_live(caches, lens, max(lens) + steps + 1)
+    first = torch.cat(firsts)
+    lengths = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    runs = []
+    for use_graph in (True, True, False):
+        lengths.copy_(torch.tensor(lens, dtype=torch.int32))
+        runs.append(eng.decode_batch(first, full, lengths, steps, use_graph=use_graph).cpu().tolist())
+        if use_graph:
+            assert len(eng._decode_graphs) == 1
+    assert runs[0] == runs[1] == runs[2]
+    eng.release_graphs()
+    assert not getattr(eng, "_decode_graphs", None)
