@@ -224,6 +224,27 @@ def test_decode_attention(ops, dtype, hq, hk, d, lens):
         torch.testing.assert_close(out[b:b + 1].float(), ref.float(), rtol=tol, atol=tol)
 
 
+@pytest.mark.parametrize("hq,hk,d,lens", [(32, 32, 128, [300]), (64, 8, 128, [1000, 3]),
+                                          (16, 2, 128, [700, 5, 260]), (32, 4, 64, [513])])
+def test_decode_attention_few_tiles_stale_workspace(ops, hq, hk, d, lens):
+    """Fewer 128-key tiles than SMs leave some CTAs without work; the merge of runs cut across
+    CTAs must not read their (never written) partial slots. The scratch is filled with NaN
+    first so a stale slot would show."""
+    dt = torch.bfloat16
+    B, cap = len(lens), max(lens) + 3
+    g = torch.Generator().manual_seed(sum(lens) + hq)
+    q = torch.randn(B, hq, d, generator=g).to(dt)
+    cache = torch.randn(B, cap, 2, hk, d, generator=g).to(dt)
+    seq = torch.tensor(lens, dtype=torch.int32)
+    nbytes = ops.decode_workspace_bytes(B, hq, d, cap)
+    ops.workspace(nbytes).view(torch.uint8).fill_(0xFF)  # NaN bit patterns everywhere
+    out = ops.decode_attention(q.cuda(), cache.cuda(), seq.cuda(), hk, cap, d ** -0.5).cpu()
+    assert torch.isfinite(out.float()).all()
+    for b, L in enumerate(lens):
+        ref = flash_attention(q[b:b + 1, None], cache[b:b + 1, :L], False, d ** -0.5)[:, 0]
+        torch.testing.assert_close(out[b:b + 1].float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
 # ------------------------------------------------------------------------------ argmax
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_argmax_ties_first_index(ops, dtype):
