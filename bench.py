@@ -127,7 +127,7 @@ def kernel_work(cfg: dict, lens: list[int], out_len: int, steps: int) -> dict:
     per layer (causal)."""
     h, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"]
     hq, hk = cfg["num_attention_heads"], cfg["num_key_value_heads"]
-    d = h // hq
+    d = cfg.get("head_dim") or h // hq
     B = len(lens)
     layer_params = (hq + 2 * hk) * d * h + h * hq * d + 2 * I * h + h * I
     dec_bytes = 0

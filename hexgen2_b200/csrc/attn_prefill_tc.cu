@@ -9,11 +9,14 @@
 //   warp 0      TMA: the Q tile once, then K/V tiles of 128 keys straight out of the KV cache
 //               ([B, max_seq, 2, hkv, d], a 4D tensor map) into a 2-stage ring.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into a double-buffered TMEM score tile
-//               (M=128, N=128, K=d); O_j = P_j V_j into a TMEM output tile (M=128, N=d, K=128,
-//               V read MN-major). S_{j+1} is issued before O_j, so QK^T overlaps the softmax.
+//               (M=128, N=128, K=d); O_j = P_j V_j into a double-buffered TMEM output tile
+//               (M=128, N=d, K=128, V read MN-major). S_{j+1} is issued before O_j, so QK^T
+//               overlaps the softmax.
 //   warps 2-5   softmax + epilogue: thread = query row. Two tcgen05.ld passes over the score
-//               row (max, then exp2/sum), P written to shared memory in the SW128 K-major
-//               layout the MMA reads, O_j accumulated in registers with the online rescale.
+//               row (max, then exp2/sum; tiles below the causal diagonal skip the mask), P
+//               written to a double-buffered shared-memory tile in the SW128 K-major layout the
+//               MMA reads; O_j is added to the register accumulator (online rescale) after the
+//               softmax of tile j+1, so that softmax runs while the tensor core computes O_j.
 // Cache rows past the live range may hold stale bits; their scores are masked to -inf and
 // their V rows are zeroed in shared memory before P.V so 0 * stale never reaches the MMA.
 #include "common.cuh"
@@ -31,9 +34,10 @@ struct Lay {
   static constexpr int kK0 = kChunks * kChunkBytes;
   static constexpr int kKV = 2 * kChunks * kChunkBytes;  // K + V of one stage
   static constexpr int kP = kK0 + 2 * kKV;
-  static constexpr int kBar = kP + 2 * kChunkBytes;
+  static constexpr int kPBytes = 2 * kChunkBytes;         // one [128 x 128 keys] P tile
+  static constexpr int kBar = kP + 2 * kPBytes;           // P[2]
   static constexpr size_t kSmem = kBar + 256 + 1024;
-  static constexpr uint32_t kTmemCols = 512;  // S[2] (256) + O (d)
+  static constexpr uint32_t kTmemCols = 512;  // S[2] (256) + O[2] (2 x d)
   static constexpr uint32_t kOCol = 256;
 };
 
@@ -58,11 +62,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_full = bars + 10;
-  uint64_t* o_empty = bars + 11;
-  uint64_t* drain = bars + 12;  // MMA completion barrier used on exit
-  uint32_t* counters = reinterpret_cast<uint32_t*>(bars + 13);  // [0] kv issued [1] kv consumed [2] q consumed
+  uint64_t* p_full = bars + 9;   // [2]
+  uint64_t* o_full = bars + 11;  // [2]
+  uint64_t* o_empty = bars + 13; // [2]
+  uint64_t* drain = bars + 15;  // MMA completion barrier used on exit
+  uint32_t* counters = reinterpret_cast<uint32_t*>(bars + 16);  // [0] kv issued [1] kv consumed [2] q consumed
   uint32_t* tmem_slot = counters + 3;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,9 +89,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
-    mbar_init(o_empty, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
+    }
     mbar_init(drain, 1);
     counters[0] = counters[1] = counters[2] = 0;
     fence_mbar_init();
@@ -151,22 +157,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && n_tiles > 0) ok = issue_s(0);
       for (int j = 0; ok && j < n_tiles; ++j) {
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1)) break;
-        if (!mbar_wait(o_empty, (j & 1) ^ 1)) break;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) break;
+        if (!mbar_wait(&o_empty[j & 1], ((j >> 1) & 1) ^ 1)) break;
         tc_fence_after();
         const int st = j & 1;
-        const uint32_t pa = smem_u32(sm + L::kP);
+        const uint32_t pa = smem_u32(sm + L::kP + (j & 1) * L::kPBytes);
         const uint32_t va = smem_u32(sm + L::kK0 + st * L::kKV + L::kChunks * kChunkBytes);
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int key = kc * 64 + k * 16;
-            tc_mma_f16(tmem + L::kOCol, sw128_kmajor_desc(pa + kc * kChunkBytes + k * 32),
+            tc_mma_f16(tmem + L::kOCol + (j & 1) * D, sw128_kmajor_desc(pa + kc * kChunkBytes + k * 32),
                        sw128_mnmajor_desc(va + key * 128, kChunkBytes, 1024), idesc_o,
                        (kc | k) ? 1u : 0u);
           }
-        tc_commit(o_full);
+        tc_commit(&o_full[j & 1]);
         tc_commit(&kv_empty[st]);
       }
       // No MMA of this CTA may still be running when TMEM is freed.
@@ -184,30 +190,58 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int e = 0; e < D; ++e) o_acc[e] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
-    uint8_t* pbase = sm + L::kP;
     bool ok = true;
+    // O_j (the P.V of tile j) is added to the register accumulator after the softmax of tile
+    // j + 1, so that softmax overlaps the P.V MMA; alpha_prev is tile j's rescale factor.
+    float alpha_prev = 1.f;
+    auto correct = [&](int jj, float al) -> bool {
+      if (!mbar_wait_warp(&o_full[jj & 1], (jj >> 1) & 1)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + L::kOCol + (jj & 1) * D + c * 32, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * al + __uint_as_float(v[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[jj & 1]);
+      return true;
+    };
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int sb = j & 1;
+      uint8_t* pbase = sm + L::kP + (j & 1) * L::kPBytes;
       if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
       const int key0 = j * kRows;
-      // Pass 1: row max over valid keys.
+      // Tiles wholly inside the live range and below the causal diagonal of every row of this
+      // CTA need no mask (all but the last tile or two of a row block).
+      const bool full = key0 + kRows <= key_end && (!a.causal || key0 + kRows - 1 <= p0 + q0);
+      // Pass 1: row max over valid keys (scale > 0, so max(s) * scale = max(s * scale)).
       float tmax = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
         tc_wait_ld();
+        if (full) {
+          float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = key0 + c * 32 + i;
-          const bool valid = key < key_end && (!a.causal || key <= qpos);
-          if (valid) tmax = fmaxf(tmax, __uint_as_float(v[i]) * a.scale_log2);
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+          tmax = fmaxf(tmax, mx * a.scale_log2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = key0 + c * 32 + i;
+            const bool valid = key < key_end && (!a.causal || key <= qpos);
+            if (valid) tmax = fmaxf(tmax, __uint_as_float(v[i]) * a.scale_log2);
+          }
         }
       }
       const float m_new = fmaxf(m_run, tmax);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m_run - m_use);
+      const float alpha = ex2_approx(m_run - m_use);
       // Pass 2: probabilities -> P (swizzled K-major) and the row sum.
       float psum = 0.f;
 #pragma unroll 1
@@ -217,20 +251,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_ld();
 #pragma unroll
         for (int g = 0; g < 4; ++g) {  // 4 groups of 8 keys = 16 bytes of P
-          T pk[8];
+          float pf[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int col = c * 32 + g * 8 + i;
             const int key = key0 + col;
-            const bool valid = key < key_end && (!a.causal || key <= qpos);
-            const float p = valid ? exp2f(__uint_as_float(v[g * 8 + i]) * a.scale_log2 - m_use) : 0.f;
-            psum += p;
-            pk[i] = DT<T>::from_f(p);
+            const bool valid = full || (key < key_end && (!a.causal || key <= qpos));
+            pf[i] = valid ? ex2_approx(fmaf(__uint_as_float(v[g * 8 + i]), a.scale_log2, -m_use)) : 0.f;
+            psum += pf[i];
           }
+          uint4 packed;
+          packed.x = pack2<T>(pf[0], pf[1]);
+          packed.y = pack2<T>(pf[2], pf[3]);
+          packed.z = pack2<T>(pf[4], pf[5]);
+          packed.w = pack2<T>(pf[6], pf[7]);
           const int col0 = c * 32 + g * 8;
           const int kc = col0 >> 6, unit = (col0 & 63) >> 3;
           uint8_t* dst = pbase + kc * kChunkBytes + r * 128 + ((unit ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(pk);
+          *reinterpret_cast<uint4*>(dst) = packed;
         }
       }
       tc_fence_before();
@@ -248,23 +286,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
       l_run = l_run * alpha + psum;
       m_run = m_new;
-      // Accumulate O_j with the online rescale.
-      if (!mbar_wait_warp(o_full, j & 1)) { ok = false; break; }
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + L::kOCol + c * 32, v);
-        tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha + __uint_as_float(v[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(o_empty);
+      if (j > 0 && !correct(j - 1, alpha_prev)) { ok = false; break; }
+      alpha_prev = alpha;
     }
+    if (ok && n_tiles > 0 && !correct(n_tiles - 1, alpha_prev)) ok = false;
     if (ok && r < nq) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       T* orow = reinterpret_cast<T*>(a.out) + (((int64_t)b * S + q0 + r) * a.n_heads + h) * D;

@@ -364,6 +364,25 @@ HX_DEVICE float warp_max(float v) {
   return v;
 }
 
+// 2^x with the SFU's approximate exp2 (flush-to-zero): the instruction FlashAttention-2's
+// softmax compiles to. For softmax arguments (x <= 0) the result is within 2 ulp of 2^x.
+HX_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two floats rounded to nearest into one packed 32-bit pair of T (bf16 or f16), low half first.
+template <typename T> HX_DEVICE uint32_t pack2(float lo, float hi);
+template <> HX_DEVICE uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <> HX_DEVICE uint32_t pack2<__half>(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
 // The host picks the dtype-specialised kernel with this switch.

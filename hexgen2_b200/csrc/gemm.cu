@@ -395,13 +395,53 @@ HX_DEVICE float dsmem_ld_f32(uint32_t cluster_addr) {
   return v;
 }
 
-// Eight output rows at once (batch rows b[0..nr), one feature n per lane, warp-uniform rows):
-// every global load the epilogue needs (residual, rotary tables) is issued for all rows before
-// any result is computed or stored, so a group costs one memory round trip instead of eight.
-// pos_s[m] = position of batch row m (fused Wqkv epilogue only), preloaded in shared memory.
+// Epilogue inputs of eight output rows (batch rows b[0..nr), feature n of this lane): the
+// residual (RESIDUAL) or the rotary cos/sin at each row's position (QKV_ROTARY), read from
+// global memory. Split from the store so the loads can be issued while the MMAs still run.
+// pos_s[m] = position of batch row m (fused Wqkv epilogue only), in shared memory.
+template <typename T, int EPI>
+struct Epi8 {
+  float x[8], y[8];
+  int64_t pos[8];
+};
+
+template <typename T, int EPI>
+HX_DEVICE void sk_load8(const GemmArgs& a, const int (&b)[8], int nr, int n, int lane,
+                        const int* pos_s, Epi8<T, EPI>& e) {
+  if (EPI == HX_EPI_QKV_ROTARY) {
+    const QkvArgs& q = a.qkv;
+    const bool rot = n < (q.n_heads + q.n_heads_kv) * q.head_dim;
+    const int pair = (n % q.head_dim) >> 1;
+    const T* cos_t = reinterpret_cast<const T*>(q.cos);
+    const T* sin_t = reinterpret_cast<const T*>(q.sin);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      e.pos[i] = -1;
+      e.x[i] = 1.f;
+      e.y[i] = 0.f;
+      if (i < nr && b[i] < a.M && !(lane & 1) && n < a.N) {
+        e.pos[i] = pos_s[b[i]];
+        if (rot && e.pos[i] >= 0 && e.pos[i] < q.table_rows) {
+          e.x[i] = DT<T>::to_f(__ldg(cos_t + e.pos[i] * (q.head_dim / 2) + pair));
+          e.y[i] = DT<T>::to_f(__ldg(sin_t + e.pos[i] * (q.head_dim / 2) + pair));
+        }
+      }
+    }
+  } else if (EPI == HX_EPI_RESIDUAL) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      e.x[i] = 0.f;
+      if (i < nr && b[i] < a.M && n < a.N)
+        e.x[i] = DT<T>::to_f(reinterpret_cast<const T*>(a.R)[(int64_t)b[i] * a.ldr + n]);
+    }
+  }
+}
+
+// Stores eight output rows (warp-uniform rows, one feature n per lane) from their f32
+// accumulators and the inputs sk_load8 fetched.
 template <typename T, int EPI>
 HX_DEVICE void sk_store8(const GemmArgs& a, const int (&b)[8], int nr, int n, int lane,
-                         const float (&v)[8], const int* pos_s) {
+                         const float (&v)[8], const Epi8<T, EPI>& e) {
   if (EPI == HX_EPI_SWIGLU) {
     float gate[8];
 #pragma unroll
@@ -424,33 +464,18 @@ HX_DEVICE void sk_store8(const GemmArgs& a, const int (&b)[8], int nr, int n, in
     const QkvArgs& q = a.qkv;
     const int hqd = q.n_heads * q.head_dim;
     const bool rot = n < hqd + q.n_heads_kv * q.head_dim;
-    const int pair = (n % q.head_dim) >> 1;
-    const T* cos_t = reinterpret_cast<const T*>(q.cos);
-    const T* sin_t = reinterpret_cast<const T*>(q.sin);
-    int64_t pos[8];
-    T cv[8], sv[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      pos[i] = -1;
-      if (i < nr && b[i] < a.M) {
-        pos[i] = pos_s[b[i]];
-        if (rot && pos[i] >= 0 && pos[i] < q.table_rows) {
-          cv[i] = __ldg(cos_t + pos[i] * (q.head_dim / 2) + pair);
-          sv[i] = __ldg(sin_t + pos[i] * (q.head_dim / 2) + pair);
-        }
-      }
-    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (!(i < nr && b[i] < a.M)) continue;
       const int m = b[i];
-      if (pos[i] < 0 || pos[i] >= q.max_seq || pos[i] >= q.table_rows) {
+      const int64_t pos = e.pos[i];
+      if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows) {
         record_device_error(HX_DEVERR_BAD_ARGUMENT);
         continue;
       }
       float x0 = round_to<T>(v[i]), x1 = round_to<T>(other[i]);
       if (rot) {
-        const float c = DT<T>::to_f(cv[i]), sn = DT<T>::to_f(sv[i]);
+        const float c = e.x[i], sn = e.y[i];
         const float o0 = x0 * c - x1 * sn;
         const float o1 = x0 * sn + x1 * c;
         x0 = o0;
@@ -458,23 +483,16 @@ HX_DEVICE void sk_store8(const GemmArgs& a, const int (&b)[8], int nr, int n, in
       }
       const int bb = m / q.seqlen;
       T* dst = n < hqd ? reinterpret_cast<T*>(q.q_out) + (int64_t)m * hqd + n
-                       : reinterpret_cast<T*>(q.cache) + (q.cbo + bb) * q.cbs + pos[i] * q.css + (n - hqd);
+                       : reinterpret_cast<T*>(q.cache) + (q.cbo + bb) * q.cbs + pos * q.css + (n - hqd);
       T pr2[2] = {DT<T>::from_f(x0), DT<T>::from_f(x1)};
       *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(pr2);
     }
   } else {
-    float r[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      r[i] = 0.f;
-      if (EPI == HX_EPI_RESIDUAL && i < nr && b[i] < a.M && n < a.N)
-        r[i] = DT<T>::to_f(reinterpret_cast<const T*>(a.R)[(int64_t)b[i] * a.ldr + n]);
-    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (i < nr && b[i] < a.M && n < a.N) {
         float x = round_to<T>(v[i]);
-        if (EPI == HX_EPI_RESIDUAL) x += r[i];
+        if (EPI == HX_EPI_RESIDUAL) x += e.x[i];
         reinterpret_cast<T*>(a.C)[(int64_t)b[i] * a.ldc + n] = DT<T>::from_f(x);
       }
     }
@@ -527,23 +545,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   if (!(warp == 0 && lane == 0)) pdl_wait();  // the producer waits after its weight prefetch
   pdl_trigger();
+  Epi8<T, EPI> pre;  // epilogue warps: inputs of the first eight rows they store
 
   if (warp == 0) {
     if (lane == 0) {
       // The weights are not produced by earlier kernels: the first ring's worth of weight
       // tiles is requested before waiting for the previous kernel (PDL), so the stream of
       // weight bytes starts while that kernel drains. Activation tiles follow the wait.
-      const int pre = min(stages, kb1 - kb0);
-      for (int i = 0; i < pre; ++i) {
+      const int npre = min(stages, kb1 - kb0);
+      for (int i = 0; i < npre; ++i) {
         mbar_arrive_expect_tx(&full[i], kStageBytes);
         tma_load_2d(ring + i * kStageBytes, &tmW, &full[i], (kb0 + i) * BK, tile * BM);
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i)
+      for (int i = 0; i < npre; ++i)
         tma_load_2d(ring + i * kStageBytes + kWBytes, &tmX, &full[i], (kb0 + i) * BK, 0);
-      int stage = pre == stages ? 0 : pre;
-      uint32_t phase = pre == stages ? 1 : 0, issued = pre;
-      for (int kb = kb0 + pre; kb < kb1; ++kb) {
+      int stage = npre == stages ? 0 : npre;
+      uint32_t phase = npre == stages ? 1 : 0, issued = npre;
+      for (int kb = kb0 + npre; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1)) break;
         mbar_arrive_expect_tx(&full[stage], kStageBytes);
         uint8_t* st = ring + stage * kStageBytes;
@@ -594,6 +613,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pos_s[m] = q.pos_start[m / q.seqlen] + m % q.seqlen;
       named_bar_sync(2, 128);
     }
+    // The first eight rows this CTA stores: their epilogue inputs are fetched while the MMAs
+    // still run.
+    int rows0[8];
+    const int rows_all = min(BN, a.M);
+    const int nr0 = S == 1 ? min(8, rows_all) : min(8, max(0, (rows_all - split + S - 1) / S));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rows0[i] = S == 1 ? i : split + i * S;
+    sk_load8<T, EPI>(a, rows0, nr0, tile * BM + r, lane, pos_s, pre);
     const bool ready = mbar_wait_warp(tfull, 0);
     tc_fence_after();
     const bool valid = ready && kb1 > kb0;
@@ -614,7 +641,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               rows[j] = c * 16 + h * 8 + j;
               vals[j] = __uint_as_float(v[h * 8 + j]);
             }
-            sk_store8<T, EPI>(a, rows, 8, tile * BM + r, lane, vals, pos_s);
+            if (c == 0 && h == 0) {
+              sk_store8<T, EPI>(a, rows, 8, tile * BM + r, lane, vals, pre);
+            } else {
+              Epi8<T, EPI> e;
+              sk_load8<T, EPI>(a, rows, 8, tile * BM + r, lane, pos_s, e);
+              sk_store8<T, EPI>(a, rows, 8, tile * BM + r, lane, vals, e);
+            }
           }
         }
       }
@@ -659,7 +692,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (c < S) sum += v[c];
           sums[i] = sum;
         }
-        sk_store8<T, EPI>(a, bs, nr, tile * BM + r, lane, sums, pos_s);
+        if (b0 == split) {
+          sk_store8<T, EPI>(a, bs, nr, tile * BM + r, lane, sums, pre);
+        } else {
+          Epi8<T, EPI> e;
+          sk_load8<T, EPI>(a, bs, nr, tile * BM + r, lane, pos_s, e);
+          sk_store8<T, EPI>(a, bs, nr, tile * BM + r, lane, sums, e);
+        }
       }
     }
     __syncwarp();

@@ -280,7 +280,8 @@ def run_bench_disaggregated(args, bench) -> dict | None:
             k[0] += t
             k[1] += 1
         tp_cfg = dict(cfg, num_attention_heads=cfg["num_attention_heads"] // P,
-                      num_key_value_heads=cfg["num_key_value_heads"] // P)
+                      num_key_value_heads=cfg["num_key_value_heads"] // P,
+                      head_dim=cfg["hidden_size"] // cfg["num_attention_heads"])
         work = bench.kernel_work(tp_cfg, pair.lens, args.out_len, 1)
         roofs = bench.rooflines(per_kernel, {"decode_attention": work["decode_attention"]}, pk)
         roofline = roofs.get("decode_attention")
