@@ -469,6 +469,60 @@ def run_kernel(args) -> dict:
     raise ValueError(args.kernel)
 
 
+# ------------------------------------------------------------------------------------------
+# Continuous batching under Poisson arrivals (one GPU)
+# ------------------------------------------------------------------------------------------
+def run_continuous(args) -> dict:
+    """Requests arrive as a Poisson process (rate --rate per second, --requests of them;
+    prompt lengths uniform in [256, 2048], output lengths uniform in [64, 512], the distributions
+    of BASELINE config 4) and are served by ContinuousBatcher with --batch slots: admitted into
+    free slots between decode steps, one graph replay per step for all slots. Reports generated
+    tokens/s over the whole run (first arrival to last completion, wall clock) and TTFT / latency
+    percentiles."""
+    import hexgen2_b200 as hx
+
+    torch.cuda.set_device(0)
+    cfg = dict(LLAMA2_7B)
+    eng = hx.Engine.from_config(cfg, dtype="bfloat16", seed=args.seed)
+    g = torch.Generator().manual_seed(args.seed + 7)
+    n = args.requests
+    gaps = torch.empty(n, dtype=torch.float64).exponential_(args.rate, generator=g)
+    arrivals = torch.cumsum(gaps, 0).tolist()
+    plens = torch.randint(256, 2049, (n,), generator=g).tolist()
+    olens = torch.randint(64, 513, (n,), generator=g).tolist()
+    prompts = [torch.randint(0, cfg["vocab_size"], (L,), generator=g).tolist() for L in plens]
+    batcher = hx.ContinuousBatcher(eng, slots=args.batch, capacity=2048 + 512 + 16)
+    # Warm-up: a few requests at once (kernels, graph, scratch buffers).
+    hx.serve_arrivals(batcher, [(f"w{i}", prompts[i], 8, 0.0) for i in range(min(4, n))])
+    torch.cuda.synchronize()
+    reqs = [(i, prompts[i], olens[i], arrivals[i] - arrivals[0]) for i in range(n)]
+    ops_launch0 = hx.ops.LAUNCHES
+    with ClockSampler(0, enabled=args.clocks) as clocks:
+        t0 = time.perf_counter()
+        stats = hx.serve_arrivals(batcher, reqs)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    gen = sum(len(v["tokens"]) for v in stats.values())
+    ttft = sorted(v["ttft_s"] * 1e3 for v in stats.values())
+    lat = sorted((v["done_s"] - r[3]) * 1e3 for r, v in zip(reqs, (stats[r[0]] for r in reqs)))
+
+    def pct(xs, q):
+        return round(xs[min(len(xs) - 1, int(q * len(xs)))], 1)
+
+    return {"metric": "continuous batching generated tokens/s (Llama-2-7B arch, Poisson arrivals)",
+            "value": round(gen / wall, 1), "unit": "tokens/s", "n_gpus": 1, "steps": 1,
+            "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random-init weights, uniform token ids)",
+            "config": {"workload": "continuous batching, Poisson arrivals (BASELINE config 4 length "
+                                   "distributions on the Llama-2-7B arch, one GPU)",
+                       "requests": n, "rate_per_s": args.rate, "slots": args.batch,
+                       "prompt_len": "uniform [256, 2048]", "output_len": "uniform [64, 512]"},
+            "wall_s": round(wall, 2), "generated_tokens": gen,
+            "ttft_ms": {"p50": pct(ttft, 0.5), "p90": pct(ttft, 0.9), "p99": pct(ttft, 0.99)},
+            "latency_ms": {"p50": pct(lat, 0.5), "p90": pct(lat, 0.9)},
+            "gpu_launches": hx.ops.LAUNCHES - ops_launch0, "clocks": clocks.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--kernel", choices=["gemm", "decode_attention", "prefill_attention", "kv_pack"],
@@ -478,8 +532,11 @@ def main():
                          "B,hq,hkv,d,S; kv_pack: layers,hkv,d,L,B")
     ap.add_argument("--epi", choices=["none", "residual", "swiglu"], default="none")
     ap.add_argument("--iters", type=int, default=50)
-    ap.add_argument("--workload", choices=["serve", "kv_handoff"], default="serve",
-                    help="kv_handoff: the KV-cache handoff microbenchmark (70B cache geometry)")
+    ap.add_argument("--workload", choices=["serve", "kv_handoff", "continuous"], default="serve",
+                    help="kv_handoff: the KV-cache handoff microbenchmark (70B cache geometry); "
+                         "continuous: continuous batching under Poisson arrivals (one GPU)")
+    ap.add_argument("--requests", type=int, default=64, help="continuous: number of requests")
+    ap.add_argument("--rate", type=float, default=8.0, help="continuous: arrivals per second")
     ap.add_argument("--kv-batches", default="1,8,64",
                     help="kv_handoff: requests per transfer, comma separated")
     ap.add_argument("--ragged", action="store_true",
@@ -503,6 +560,8 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.kernel:
         line = run_kernel(args)
+    elif args.workload == "continuous" and args.impl == "native":
+        line = run_continuous(args)
     elif args.workload == "kv_handoff" and args.impl == "native":
         from hexgen2_b200.disagg import run_kv_bench
         line = run_kv_bench(args, sys.modules[__name__])

@@ -7,9 +7,9 @@ Public API (mirrors the reference's):
     recv_data, validate_header, KVHandoff  hexgen2/transport.py (+ the NVLink direct path)
 The compute runs in libhexgen2_b200.so (see include/hexgen2_b200.h); there is no CPU path.
 """
-from .engine import Engine
+from .engine import ContinuousBatcher, Engine, serve_arrivals
 from .gpt import CacheState, GPTLMHeadModel, InferenceParams
 from .transport import KVHandoff, recv_data, recv_packet, send_data, send_packet, validate_header
 
-__all__ = ["Engine", "CacheState", "GPTLMHeadModel", "InferenceParams", "KVHandoff",
+__all__ = ["Engine", "ContinuousBatcher", "serve_arrivals", "CacheState", "GPTLMHeadModel", "InferenceParams", "KVHandoff",
            "send_packet", "recv_packet", "send_data", "recv_data", "validate_header"]

@@ -195,7 +195,7 @@ class Engine:
 
     @torch.inference_mode()
     def decode_batch(self, first_tokens: torch.Tensor, caches: dict, lengths: torch.Tensor,
-                     steps: int, use_graph: bool = True):
+                     steps: int, use_graph: bool = True, capture_first: bool = False):
         """Greedy decode of a ragged batch without host syncs: first_tokens [B] (device int64),
         caches {layer: [B, capacity, 2, hkv, d]} holding lengths[b] live rows per sequence
         (lengths: int32 device [B], advanced in place). Returns tokens [B, steps + 1] on the
@@ -206,7 +206,9 @@ class Engine:
         is part of the graph, so a step is one launch from the host. The graph is kept per
         (batch, cache, lengths, scratch buffers, rotary tables) and replayed by later calls on
         the same buffers; the first call runs one step eagerly (it also sizes every scratch
-        buffer) and captures."""
+        buffer) and captures. With capture_first (for callers that already ran a step on these
+        buffers, so every scratch buffer is sized), a missing graph is captured at the first
+        step instead, so even single-step calls replay."""
         B = first_tokens.numel()
         capacity = caches[0].shape[1]
         tokens = torch.empty(steps + 1, B, dtype=torch.long, device=self.device)
@@ -241,7 +243,8 @@ class Engine:
             if entry is not None:
                 graph.replay()
                 ops.LAUNCHES += per_replay  # kernels of this library inside one replay
-            elif use_graph and s >= 1 and (steps - s > 1 or not profiling):
+            elif use_graph and (s >= 1 or (capture_first and not profiling)) and (
+                    steps - s > 1 or not profiling):
                 graph = torch.cuda.CUDAGraph()
                 before = ops.LAUNCHES
                 mark = len(ops.PROFILE) if profiling else 0
@@ -303,3 +306,112 @@ class Engine:
     def synchronize(self):
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
+
+
+class ContinuousBatcher:
+    """Continuous batching on one engine: a fixed pool of `slots` sequences in one all-layer
+    cache [layers, slots, capacity, 2, hkv, d]. Every step decodes all slots with one replay
+    of the kept decode graph (ragged per-slot lengths); a finished request frees its slot at
+    once, and waiting requests are prefilled straight into free slots between steps. Idle
+    slots sit at length 0 (their step attends to one key and is discarded).
+
+    The reference batches by padding every cache to the longest one and decoding the padded
+    batch until all requests end (hexgen/llama/kv_cache_batch.py:4-29,
+    inference_phases.py:141-212); here requests join and leave per step, and each request's
+    tokens equal its batch-1 greedy decode.
+    """
+
+    def __init__(self, engine: Engine, slots: int, capacity: int):
+        self.eng, self.slots, self.capacity = engine, slots, capacity
+        dev = engine.device
+        self.cache = engine.model.allocate_inference_cache(slots, capacity)
+        self.lengths = torch.zeros(slots, dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros(slots, dtype=torch.long, device=dev)
+        self.req = [None] * slots        # request id per slot
+        self.left = [0] * slots          # tokens still to generate per slot
+        self.out: dict = {}              # request id -> generated tokens
+        # Capture the decode graph once on the idle pool; later steps only replay it.
+        self.eng.decode_batch(self.tokens, self.cache, self.lengths, 2)
+        self.lengths.zero_()
+
+    def free_slots(self) -> list[int]:
+        return [i for i, r in enumerate(self.req) if r is None]
+
+    def active(self) -> int:
+        return sum(r is not None for r in self.req)
+
+    @torch.inference_mode()
+    def admit(self, req_id, prompt: list[int], max_new_tokens: int) -> int:
+        """Prefills `prompt` into a free slot; returns the first generated token (greedy)."""
+        free = self.free_slots()
+        if not free:
+            raise ValueError("no free slot")
+        L = len(prompt)
+        if L + max_new_tokens > self.capacity:
+            raise ValueError(f"request needs {L + max_new_tokens} positions, capacity {self.capacity}")
+        slot = free[0]
+        ids = torch.tensor([prompt], dtype=torch.long, device=self.eng.device)
+        st = CacheState(self.capacity, max_batch_size=self.slots, batch_size_offset=slot,
+                        key_value_memory_dict=self.cache)
+        logits = self.eng.model(ids, inference_params=st, last_token_only=True).logits
+        ops.argmax(logits, out=self.tokens[slot:slot + 1])
+        self.lengths[slot:slot + 1].fill_(L)
+        first = int(self.tokens[slot].item())
+        self.req[slot], self.left[slot] = req_id, max_new_tokens - 1
+        self.out[req_id] = [first]
+        if self.left[slot] == 0:
+            self._retire(slot)
+        return first
+
+    def _retire(self, slot: int):
+        self.req[slot] = None
+        self.lengths[slot:slot + 1].zero_()
+
+    @torch.inference_mode()
+    def step(self) -> list:
+        """One decode step for every slot; returns the ids of requests that finished."""
+        toks = self.eng.decode_batch(self.tokens, self.cache, self.lengths, 1, capture_first=True)
+        new = toks[:, 1].contiguous()
+        self.tokens.copy_(new)
+        host = new.tolist()
+        done = []
+        for slot, rid in enumerate(self.req):
+            if rid is None:
+                continue
+            self.out[rid].append(host[slot])
+            self.left[slot] -= 1
+            if self.left[slot] == 0:
+                self._retire(slot)
+                done.append(rid)
+        return done
+
+
+def serve_arrivals(batcher: ContinuousBatcher, requests: list, clock=None) -> dict:
+    """Serves requests [(req_id, prompt, max_new_tokens, arrival_s)] as they arrive (wall clock
+    from the first call), admitting into free slots between decode steps. Returns per request
+    {"tokens", "ttft_s", "done_s"} (times relative to the start)."""
+    import time
+    clock = clock or time.perf_counter
+    t0 = clock()
+    pending = sorted(requests, key=lambda r: r[3])
+    stats, arrival = {}, {r[0]: r[3] for r in requests}
+    i = 0
+    while i < len(pending) or batcher.active():
+        now = clock() - t0
+        while i < len(pending) and pending[i][3] <= now and batcher.free_slots():
+            rid, prompt, max_new, _ = pending[i]
+            batcher.admit(rid, prompt, max_new)
+            stats[rid] = {"ttft_s": clock() - t0 - arrival[rid]}
+            if batcher.req.count(rid) == 0:  # finished at its first token
+                stats[rid]["done_s"] = clock() - t0
+            i += 1
+        if batcher.active():
+            for rid in batcher.step():
+                stats[rid]["done_s"] = clock() - t0
+        elif i < len(pending):
+            wait = pending[i][3] - (clock() - t0)
+            if wait > 0:
+                time.sleep(min(wait, 0.01))
+    for rid in stats:
+        stats[rid]["tokens"] = batcher.out[rid]
+    return stats

@@ -253,3 +253,114 @@ class KVHandoff:
         if self._mapped:
             self._lib.lib().hx_ipc_close_handle(self._mapped)
             self._mapped = None
+
+
+# ------------------------------------------------------------------------------------------
+# KV re-sharding between groups of different tensor-parallel sizes
+# ------------------------------------------------------------------------------------------
+def reshard_plan(n_kv_heads: int, src_tp: int, dst_tp: int) -> list[tuple[int, int, int, int]]:
+    """Slice moves that turn a cache sharded over src_tp ranks (rank i holds KV heads
+    [i*h/src_tp, (i+1)*h/src_tp)) into one sharded over dst_tp ranks: a list of
+    (src_rank, dst_rank, head_lo, head_hi) in global head indices, by destination rank then head.
+    The reference concatenates all shards on the head dimension and would then split
+    (hexgen/llama/tensor_parallel_dim_concat.py:9-21); these moves give the same per-rank caches
+    without materialising the full one. Raises ValueError if a TP size does not divide the heads."""
+    if src_tp <= 0 or dst_tp <= 0 or n_kv_heads % src_tp or n_kv_heads % dst_tp:
+        raise ValueError(f"{n_kv_heads} KV heads cannot be split {src_tp} and {dst_tp} ways")
+    hs, hd = n_kv_heads // src_tp, n_kv_heads // dst_tp
+    plan = []
+    for dst in range(dst_tp):
+        lo, hi = dst * hd, (dst + 1) * hd
+        for src in range(src_tp):
+            a, b = max(lo, src * hs), min(hi, (src + 1) * hs)
+            if a < b:
+                plan.append((src, dst, a, b))
+    return plan
+
+
+def _cache_geometry(caches: dict):
+    """(layer-0 view, layers, layer stride in bytes) of an engine's all-layer cache handed out
+    as per-layer views {layer: [B, cap, 2, hkv, d]}."""
+    n = len(caches)
+    big0 = caches[0]
+    stride = (caches[1].data_ptr() - big0.data_ptr()) if n > 1 else 0
+    if any(caches[i].data_ptr() != big0.data_ptr() + i * stride for i in range(n)):
+        raise ValueError("expected one all-layer cache (per-layer views at a fixed stride)")
+    if big0.stride(-1) != 1 or big0.stride(-2) != big0.shape[-1]:
+        raise ValueError("cache rows must be contiguous [2, hkv, d]")
+    return big0, n, stride
+
+
+def head_slice_bytes(caches: dict, lengths: list[int], n_heads: int) -> list[int]:
+    """Packed bytes per request of a head slice (K slab then V slab, all layers)."""
+    big0, n, _ = _cache_geometry(caches)
+    return [2 * n * L * n_heads * big0.shape[-1] * big0.element_size() for L in lengths]
+
+
+def pack_kv_heads(caches: dict, rows: list[int], lengths: list[int], head_lo: int, head_hi: int,
+                  dst, dst_offsets: list[int]):
+    """Gather-packs KV heads [head_lo, head_hi) (indices local to this cache) of the live rows
+    of requests `rows` (batch rows of the all-layer cache) into `dst` (a CUDA tensor, or a peer
+    address from KVHandoff.attach): per request, at dst_offsets[r], the K slab
+    [layers][L][heads][d] followed by the V slab. Two gather-pack launches (K, V)."""
+    from . import ops
+    big0, n, lstride = _cache_geometry(caches)
+    hk, d, elem = big0.shape[-2], big0.shape[-1], big0.element_size()
+    if not 0 <= head_lo < head_hi <= hk:
+        raise ValueError(f"head range [{head_lo}, {head_hi}) outside the cache's {hk} heads")
+    nh = head_hi - head_lo
+    dev = big0.device
+    slab = [n * L * nh * d * elem for L in lengths]
+    live = torch.tensor(lengths, dtype=torch.int64, device=dev)
+    for part, head0 in ((0, head_lo), (1, hk + head_lo)):
+        src = torch.tensor([big0.data_ptr() + (r * big0.stride(0) + head0 * d) * elem for r in rows],
+                           dtype=torch.int64, device=dev)
+        offs = torch.tensor([o + part * s for o, s in zip(dst_offsets, slab)], dtype=torch.int64,
+                            device=dev)
+        ops.kv_pack(src, live, offs, n, lstride, big0.stride(1) * elem, nh * d * elem,
+                    max(lengths), dst)
+
+
+def unpack_kv_heads(src, src_offsets: list[int], caches: dict, rows: list[int],
+                    lengths: list[int], head_lo: int, head_hi: int):
+    """Inverse of pack_kv_heads: scatters packed head slices into heads [head_lo, head_hi) of the
+    live rows of requests `rows` of this all-layer cache."""
+    from . import ops
+    big0, n, lstride = _cache_geometry(caches)
+    hk, d, elem = big0.shape[-2], big0.shape[-1], big0.element_size()
+    if not 0 <= head_lo < head_hi <= hk:
+        raise ValueError(f"head range [{head_lo}, {head_hi}) outside the cache's {hk} heads")
+    nh = head_hi - head_lo
+    dev = big0.device
+    slab = [n * L * nh * d * elem for L in lengths]
+    live = torch.tensor(lengths, dtype=torch.int64, device=dev)
+    for part, head0 in ((0, head_lo), (1, hk + head_lo)):
+        dst = torch.tensor([big0.data_ptr() + (r * big0.stride(0) + head0 * d) * elem for r in rows],
+                           dtype=torch.int64, device=dev)
+        offs = torch.tensor([o + part * s for o, s in zip(src_offsets, slab)], dtype=torch.int64,
+                            device=dev)
+        ops.kv_unpack(src, offs, live, dst, n, lstride, big0.stride(1) * elem, nh * d * elem,
+                      max(lengths))
+
+
+def reshard_kv(src_caches: list[dict], dst_caches: list[dict], rows: list[int],
+               lengths: list[int], n_kv_heads: int):
+    """Moves the live rows of requests `rows` from caches sharded over len(src_caches) TP ranks
+    into caches sharded over len(dst_caches) ranks, all on this process's devices: for every
+    move of reshard_plan, one pack into a staging buffer on the source's device and one unpack
+    into the destination (peer reads when the two differ). Across processes the same moves run
+    with the staging buffer exposed through KVHandoff."""
+    src_tp, dst_tp = len(src_caches), len(dst_caches)
+    hs, hd = n_kv_heads // src_tp, n_kv_heads // dst_tp
+    for s, t, lo, hi in reshard_plan(n_kv_heads, src_tp, dst_tp):
+        nh = hi - lo
+        sizes = head_slice_bytes(src_caches[s], lengths, nh)
+        offs, o = [], 0
+        for b in sizes:
+            offs.append(o)
+            o += (b + 15) // 16 * 16
+        staging = torch.empty(max(o, 16), dtype=torch.uint8, device=src_caches[s][0].device)
+        pack_kv_heads(src_caches[s], rows, lengths, lo - s * hs, hi - s * hs, staging, offs)
+        if staging.device != dst_caches[t][0].device:
+            staging = staging.to(dst_caches[t][0].device)
+        unpack_kv_heads(staging, offs, dst_caches[t], rows, lengths, lo - t * hd, hi - t * hd)

@@ -16,6 +16,7 @@ What it restates (paths inside the HexGen-2 project):
   * CrossAttention (CPU attention) ... hexgen/hexgen_core/modules/mha.py:209-244
   * GatedMlp ......................... hexgen/hexgen_core/modules/mlp.py:79-87
   * Engine.prefill / Engine.decode ... hexgen2/model.py:70-121
+  * TP-shard concat of KV caches ..... hexgen/llama/tensor_parallel_dim_concat.py:9-21
 Third-party arithmetic restated from its published algorithm (flash-attn 2.7.4.post1, git
 5231d95fe13733fb534c01895f7ea88c6a6c7793, pinned by scripts/fabric/setup.sh:52-54):
   * RotaryEmbedding: inv_freq = 1/base^(arange(0,d,2)/d) in f32, cos/sin of outer(t, inv_freq)
@@ -330,3 +331,10 @@ def load_hf_checkpoint(folder, dtype=torch.float32):
     for shard in sorted(folder.glob("*.safetensors")):
         state.update(load_file(str(shard), device="cpu"))
     return shape, remap_hf_to_native(state, shape)
+
+
+def concat_kv_heads(shards: list[dict], dim: int = 3) -> dict:
+    """hexgen/llama/tensor_parallel_dim_concat.py:9-21 (concat_dicts): the per-layer caches of
+    the tensor-parallel shards, [B, S, 2, heads/tp, d] each, concatenated on the head dimension
+    (dim 3) in rank order."""
+    return {k: torch.cat([d[k] for d in shards], dim=dim) for k in shards[0]}

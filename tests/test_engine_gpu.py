@@ -228,3 +228,23 @@ def test_decode_graph_is_kept_and_replayed(hx):
     assert runs[0] == runs[1] == runs[2]
     eng.release_graphs()
     assert not getattr(eng, "_decode_graphs", None)
+
+
+def test_continuous_batching_matches_batch1_greedy(hx):
+    """Six requests through three slots (requests join as slots free up, one finishes at its
+    first token): every request's tokens equal its own batch-1 prefill + greedy decode."""
+    oracle, eng = _oracle_and_engine(hx, dict(TINYLLAMA, vocab_size=4096), 2, torch.bfloat16, seed=7)
+    g = torch.Generator().manual_seed(9)
+    reqs = [(i, torch.randint(0, 4096, (L,), generator=g).tolist(), n)
+            for i, (L, n) in enumerate([(5, 7), (40, 3), (17, 12), (3, 1), (64, 9), (9, 6)])]
+    expected = {}
+    for rid, prompt, n in reqs:
+        f, c, _ = eng.prefill(prompt, n)
+        expected[rid] = eng.decode(f, c, len(prompt), n)
+    batcher = hx.ContinuousBatcher(eng, slots=3, capacity=80)
+    stats = hx.serve_arrivals(batcher, [(rid, p, n, 0.0) for rid, p, n in reqs])
+    for rid, p, n in reqs:
+        assert stats[rid]["tokens"] == expected[rid], rid
+        assert stats[rid]["ttft_s"] >= 0 and stats[rid]["done_s"] >= stats[rid]["ttft_s"]
+    assert batcher.active() == 0 and len(batcher.free_slots()) == 3
+    assert len(eng._decode_graphs) == 1  # one kept graph served every step

@@ -245,6 +245,42 @@ def test_decode_attention_few_tiles_stale_workspace(ops, hq, hk, d, lens):
         torch.testing.assert_close(out[b:b + 1].float(), ref.float(), rtol=2e-2, atol=2e-2)
 
 
+# ------------------------------------------------------------------------------ KV re-shard
+@pytest.mark.parametrize("src_tp,dst_tp", [(2, 4), (4, 2), (2, 1), (1, 8)])
+def test_reshard_kv_matches_reference_head_concat(ops, src_tp, dst_tp):
+    """Prefill TP != decode TP: the per-rank caches after the slice moves equal the reference's
+    concat of the shards on the head dimension (tensor_parallel_dim_concat.py), split dst_tp
+    ways. Bytes compared exactly."""
+    from oracle.llama_ref import concat_kv_heads
+    from hexgen2_b200.transport import reshard_kv
+    layers, B, cap, H, d = 3, 3, 60, 8, 64
+    lens = [17, 60, 1]
+    rows = [2, 0, 1]  # request r lives in batch row rows[r]
+    g = torch.Generator().manual_seed(src_tp * 10 + dst_tp)
+    full = torch.randn(layers, B, cap, 2, H, d, generator=g).bfloat16()
+    hs, hd = H // src_tp, H // dst_tp
+    src = []
+    for s in range(src_tp):
+        shard = full[:, :, :, :, s * hs:(s + 1) * hs].contiguous().cuda()
+        src.append({i: shard[i] for i in range(layers)})
+    dst = []
+    for t in range(dst_tp):
+        big = torch.zeros(layers, B, cap, 2, hd, d, dtype=torch.bfloat16, device="cuda")
+        dst.append({i: big[i] for i in range(layers)})
+    reshard_kv(src, dst, rows, lens, H)
+    torch.cuda.synchronize()
+    for r, (row, L) in enumerate(zip(rows, lens)):
+        shards = [{i: src[s][i][row:row + 1, :L].cpu() for i in range(layers)} for s in range(src_tp)]
+        whole = concat_kv_heads(shards)
+        for t in range(dst_tp):
+            for i in range(layers):
+                want = whole[i][..., t * hd:(t + 1) * hd, :]
+                got = dst[t][i][row:row + 1, :L].cpu()
+                assert torch.equal(got, want)
+                # rows past the live length stay untouched
+                assert not dst[t][i][row, L:].abs().sum().item()
+
+
 # ------------------------------------------------------------------------------ argmax
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_argmax_ties_first_index(ops, dtype):

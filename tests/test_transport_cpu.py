@@ -97,3 +97,24 @@ def _fault_worker(rank, rendezvous):
 
 def test_bad_header_length_rejected_on_real_ranks(tmp_path):
     mp.spawn(_fault_worker, args=(str(tmp_path / "rv"),), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("heads,src,dst", [(8, 2, 4), (8, 4, 2), (8, 2, 1), (8, 1, 8), (32, 4, 2), (6, 3, 2)])
+def test_reshard_plan_covers_every_head_once(heads, src, dst):
+    from hexgen2_b200.transport import reshard_plan
+    plan = reshard_plan(heads, src, dst)
+    seen = []
+    for s, t, lo, hi in plan:
+        assert s * (heads // src) <= lo < hi <= (s + 1) * (heads // src)  # inside the source shard
+        assert t * (heads // dst) <= lo < hi <= (t + 1) * (heads // dst)  # inside the dest shard
+        seen.extend(range(lo, hi))
+    assert sorted(seen) == list(range(heads))
+    assert [p[1] for p in plan] == sorted(p[1] for p in plan)
+
+
+def test_reshard_plan_rejects_indivisible_sizes():
+    from hexgen2_b200.transport import reshard_plan
+    with pytest.raises(ValueError):
+        reshard_plan(8, 3, 2)
+    with pytest.raises(ValueError):
+        reshard_plan(8, 2, 0)
