@@ -418,6 +418,29 @@ def run_kernel(args) -> dict:
                 "GB/s": round(gbs, 1), "TFLOP/s": round(tfs, 1), "bound": bound,
                 "frac": round(achieved / peak, 4), "peak_source": pk["source"],
                 "l2": f"{copies} weight copies rotated"}
+    if args.kernel == "gemm_qkv":
+        # Wqkv projection with rotary + KV-cache write fused into the epilogue (decode rows,
+        # one token per sequence at positions around 1000).
+        M, hq, hk, d = (int(v) for v in args.shape.split(","))
+        h, N = hq * d, (hq + 2 * hk) * d
+        wbytes = N * h * 2
+        copies = max(1, min(64, -(-3 * l2 // wbytes)))
+        ws = [torch.randn(N, h, generator=g, device="cuda", dtype=dt) * 0.02 for _ in range(copies)]
+        x = torch.randn(M, h, generator=g, device="cuda", dtype=dt)
+        cap = 1200
+        pos = torch.randint(900, 1100, (M,), generator=g, device="cuda", dtype=torch.int32)
+        ang = torch.arange(cap, device="cuda", dtype=torch.float32)[:, None] * \
+            (1.0 / 10000 ** (torch.arange(0, d, 2, device="cuda", dtype=torch.float32) / d))
+        cos, sin = ang.cos().to(dt).contiguous(), ang.sin().to(dt).contiguous()
+        cache = torch.empty(M, cap, 2, hk, d, device="cuda", dtype=dt)
+        q_out = torch.empty(M, hq, d, device="cuda", dtype=dt)
+        us = timed(lambda i: ops.gemm_qkv_rotary(x, ws[i % copies], 1, hq, hk, d, pos, cos, sin,
+                                                 cache, q_out=q_out), iters)
+        nbytes = wbytes + M * h * 2 + M * N * 2
+        gbs = nbytes / us / 1e3
+        return {"kernel": "gemm_qkv_rotary", "shape": [M, hq, hk, d], "us": round(us, 2),
+                "GB/s": round(gbs, 1), "bound": "hbm", "frac": round(gbs / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"], "l2": f"{copies} weight copies rotated"}
     if args.kernel == "decode_attention":
         # L = live keys of every sequence, or with --ragged the mean of the bench's lognormal
         # prompt lengths plus L (mid-decode), one length per sequence.
@@ -525,10 +548,12 @@ def run_continuous(args) -> dict:
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--kernel", choices=["gemm", "decode_attention", "prefill_attention", "kv_pack"],
+    ap.add_argument("--kernel", choices=["gemm", "gemm_qkv", "decode_attention", "prefill_attention",
+                                         "kv_pack"],
                     help="time one kernel alone (shape via --shape) instead of the model step")
     ap.add_argument("--shape", default="32,4096,4096",
-                    help="gemm: M,N,K; decode_attention: B,hq,hkv,d,L; prefill_attention: "
+                    help="gemm: M,N,K; gemm_qkv: M,hq,hkv,d; decode_attention: B,hq,hkv,d,L; "
+                         "prefill_attention: "
                          "B,hq,hkv,d,S; kv_pack: layers,hkv,d,L,B")
     ap.add_argument("--epi", choices=["none", "residual", "swiglu"], default="none")
     ap.add_argument("--iters", type=int, default=50)

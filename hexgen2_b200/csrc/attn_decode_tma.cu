@@ -110,9 +110,40 @@ struct PieceWalker {
   }
 };
 
+// Issues the K and V loads of one 128-key tile into a ring stage and arms its barrier. A tile
+// with fewer live keys (the last of a run) is fetched in 32-row boxes, only as many as hold
+// live keys (SWIZZLE_128B is a function of the shared-memory address, so the partial boxes land
+// exactly where the full box would have put those rows); rows past them keep stale bytes that
+// the consumers never use.
+template <int kChunks>
+HX_DEVICE void load_kv_tile(uint8_t* kb, uint64_t* bar, const CUtensorMap* full_map,
+                            const CUtensorMap* map32, int hk, int hkv, int key0, int b,
+                            int live_rows) {
+  uint8_t* vb = kb + kChunks * kBoxBytes;
+  if (live_rows >= kTileKeys) {
+    mbar_arrive_expect_tx(bar, 2 * kChunks * kBoxBytes);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      tma_load_4d(kb + c * kBoxBytes, full_map, bar, c * 64, hk, key0, b);
+      tma_load_4d(vb + c * kBoxBytes, full_map, bar, c * 64, hkv + hk, key0, b);
+    }
+    return;
+  }
+  const int n32 = (live_rows + 31) / 32;
+  mbar_arrive_expect_tx(bar, 2 * kChunks * n32 * 32 * 128);
+  for (int i = 0; i < n32; ++i) {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      tma_load_4d(kb + c * kBoxBytes + i * 32 * 128, map32, bar, c * 64, hk, key0 + i * 32, b);
+      tma_load_4d(vb + c * kBoxBytes + i * 32 * 128, map32, bar, c * 64, hkv + hk, key0 + i * 32, b);
+    }
+  }
+}
+
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(kThreadsTma, 1)
-    decode_tma_kernel(const __grid_constant__ CUtensorMap tmKV, const DecArgs a) {
+    decode_tma_kernel(const __grid_constant__ CUtensorMap tmKV,
+                      const __grid_constant__ CUtensorMap tmKV32, const DecArgs a) {
   using L = DLay<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -128,6 +159,7 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmKV);
+    prefetch_tensormap(&tmKV32);
     for (int s = 0; s < L::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
@@ -171,14 +203,9 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
         for (int t = p.t_lo; t < p.t_hi; ++t) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) goto producer_done;
           ++issued;
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          uint8_t* kb = ring + stage * L::kStageBytes;
-          uint8_t* vb = kb + L::kChunks * kBoxBytes;
-#pragma unroll
-          for (int c = 0; c < L::kChunks; ++c) {
-            tma_load_4d(kb + c * kBoxBytes, &tmKV, &full[stage], c * 64, p.hk, t * kTileKeys, p.b);
-            tma_load_4d(vb + c * kBoxBytes, &tmKV, &full[stage], c * 64, hkv + p.hk, t * kTileKeys, p.b);
-          }
+          load_kv_tile<L::kChunks>(ring + stage * L::kStageBytes, &full[stage], &tmKV, &tmKV32,
+                                   p.hk, hkv, t * kTileKeys, p.b,
+                                   live_len(a, p.b) - t * kTileKeys);
           if (++stage == L::kStages) {
             stage = 0;
             phase ^= 1;
@@ -427,7 +454,8 @@ __global__ void decode_tma_merge_kernel(const DecArgs a, int grid) {
 }
 
 template <typename T, int D, int G>
-int launch(const CUtensorMap& map, const DecArgs& args, int grid, cudaStream_t stream) {
+int launch(const CUtensorMap& map, const CUtensorMap& map32, const DecArgs& args, int grid,
+           cudaStream_t stream) {
   using L = DLay<D>;
   const size_t smem = (size_t)L::kRing + 1024 +
                       sizeof(float) * (G * D + kConsumers * G * D + kConsumers * G * 2 + 2) +
@@ -443,7 +471,7 @@ int launch(const CUtensorMap& map, const DecArgs& args, int grid, cudaStream_t s
     if (s) return s;
     attr[dev & 63] = true;
   }
-  int s = hx::cuda_status(launch_ex(kern, dim3(grid), dim3(kThreadsTma), smem, stream, 1, map, args),
+  int s = hx::cuda_status(launch_ex(kern, dim3(grid), dim3(kThreadsTma), smem, stream, 1, map, map32, args),
                           "decode_tma_kernel launch");
   if (s) return s;
   HX_LAUNCH_CHECK("decode_tma_kernel");
@@ -539,8 +567,9 @@ struct TileWalker {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    decode_tc_kernel(const __grid_constant__ CUtensorMap tmKV, const __grid_constant__ CUtensorMap tmQ,
-                     const DecArgs a) {
+    decode_tc_kernel(const __grid_constant__ CUtensorMap tmKV,
+                     const __grid_constant__ CUtensorMap tmKV32,
+                     const __grid_constant__ CUtensorMap tmQ, const DecArgs a) {
   using L = TcLay<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -566,6 +595,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmKV);
+    prefetch_tensormap(&tmKV32);
     prefetch_tensormap(&tmQ);
     for (int s = 0; s < L::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -630,14 +660,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         const int st = j % L::kStages;
         if (!mbar_wait(&kv_empty[st], ((j / L::kStages) & 1) ^ 1)) break;
-        mbar_arrive_expect_tx(&kv_full[st], L::kStageBytes);
-        uint8_t* kb = sm + st * L::kStageBytes;
-        uint8_t* vb = kb + L::kChunks * kBoxBytes;
-#pragma unroll
-        for (int c = 0; c < L::kChunks; ++c) {
-          tma_load_4d(kb + c * kBoxBytes, &tmKV, &kv_full[st], c * 64, tw.p.hk, tw.t * kTileKeys, tw.p.b);
-          tma_load_4d(vb + c * kBoxBytes, &tmKV, &kv_full[st], c * 64, hkv + tw.p.hk, tw.t * kTileKeys, tw.p.b);
-        }
+        load_kv_tile<L::kChunks>(sm + st * L::kStageBytes, &kv_full[st], &tmKV, &tmKV32, tw.p.hk,
+                                 hkv, tw.t * kTileKeys, tw.p.b,
+                                 live_len(a, tw.p.b) - tw.t * kTileKeys);
         ++j;
       }
     }
@@ -879,8 +904,8 @@ __global__ void decode_tc_merge_kernel(const DecArgs a, int grid) {
 }
 
 template <typename T, int D>
-int launch_tc(const CUtensorMap& map, const CUtensorMap& qmap, const DecArgs& args, int grid,
-              cudaStream_t stream) {
+int launch_tc(const CUtensorMap& map, const CUtensorMap& map32, const CUtensorMap& qmap,
+              const DecArgs& args, int grid, cudaStream_t stream) {
   using L = TcLay<D>;
   auto kern = decode_tc_kernel<T, D>;
   static bool attr[64] = {false};
@@ -893,7 +918,7 @@ int launch_tc(const CUtensorMap& map, const CUtensorMap& qmap, const DecArgs& ar
     if (s) return s;
     attr[dev & 63] = true;
   }
-  int s = hx::cuda_status(launch_ex(kern, dim3(grid), dim3(kTcThreads), L::kSmem, stream, 1, map, qmap, args),
+  int s = hx::cuda_status(launch_ex(kern, dim3(grid), dim3(kTcThreads), L::kSmem, stream, 1, map, map32, qmap, args),
                           "decode_tc_kernel launch");
   if (s) return s;
   HX_LAUNCH_CHECK("decode_tc_kernel");
@@ -939,6 +964,10 @@ int decode_attention_tma(const void* q, const void* cache, int64_t cbs, int64_t 
   const uint32_t box[4] = {64, 1, (uint32_t)kTileKeys, 1};
   int s = make_tensor_map(&map, cache, 4, dims, strides, box, dtype);
   if (s) return s;
+  CUtensorMap map32;  // 32-row boxes for the partial last tile of a run
+  const uint32_t box32[4] = {64, 1, 32, 1};
+  s = make_tensor_map(&map32, cache, 4, dims, strides, box32, dtype);
+  if (s) return s;
   const int grid = device_sm_count();
   const int64_t slots = 2 * (int64_t)grid;
   float* ws_o = (float*)ws;
@@ -955,12 +984,12 @@ int decode_attention_tma(const void* q, const void* cache, int64_t cbs, int64_t 
     s = make_tensor_map(&qmap, q, 2, qdims, qstrides, qbox, dtype);
     if (s) return s;
     if (dtype == HX_BF16)
-      return head_dim == 128 ? launch_tc<__nv_bfloat16, 128>(map, qmap, args, grid, stream)
-                             : launch_tc<__nv_bfloat16, 64>(map, qmap, args, grid, stream);
-    return head_dim == 128 ? launch_tc<__half, 128>(map, qmap, args, grid, stream)
-                           : launch_tc<__half, 64>(map, qmap, args, grid, stream);
+      return head_dim == 128 ? launch_tc<__nv_bfloat16, 128>(map, map32, qmap, args, grid, stream)
+                             : launch_tc<__nv_bfloat16, 64>(map, map32, qmap, args, grid, stream);
+    return head_dim == 128 ? launch_tc<__half, 128>(map, map32, qmap, args, grid, stream)
+                           : launch_tc<__half, 64>(map, map32, qmap, args, grid, stream);
   }
-#define HX_DEC_TMA(TT, DD, GG) return launch<TT, DD, GG>(map, args, grid, stream)
+#define HX_DEC_TMA(TT, DD, GG) return launch<TT, DD, GG>(map, map32, args, grid, stream)
   if (dtype == HX_BF16) {
     if (head_dim == 128) { if (group == 1) HX_DEC_TMA(__nv_bfloat16, 128, 1); HX_DEC_TMA(__nv_bfloat16, 128, 2); }
     if (group == 1) HX_DEC_TMA(__nv_bfloat16, 64, 1);
