@@ -70,7 +70,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = counters + 3;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // Heads vary fastest and query blocks run last-to-first, so under a causal mask the CTAs with
+  // the most key tiles start in the first wave and the light ones fill the tail.
+  const int h = blockIdx.x, qblk = gridDim.y - 1 - blockIdx.y, b = blockIdx.z;
   const int S = a.seqlen_q;
   const int q0 = qblk * kRows;
   const int nq = min(kRows, S - q0);
@@ -226,9 +228,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
         tc_wait_ld();
         if (full) {
-          float mx = -INFINITY;
+          // Tree of independent maxima (a 5-deep chain instead of 32).
+          float m8[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+          for (int k = 0; k < 8; ++k)
+            m8[k] = fmaxf(fmaxf(__uint_as_float(v[k]), __uint_as_float(v[k + 8])),
+                          fmaxf(__uint_as_float(v[k + 16]), __uint_as_float(v[k + 24])));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) m8[k] = fmaxf(m8[k], m8[k + 4]);
+          const float mx = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
           tmax = fmaxf(tmax, mx * a.scale_log2);
         } else {
 #pragma unroll
@@ -242,8 +250,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_new = fmaxf(m_run, tmax);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2_approx(m_run - m_use);
-      // Pass 2: probabilities -> P (swizzled K-major) and the row sum.
-      float psum = 0.f;
+      // Pass 2: probabilities -> P (swizzled K-major) and the row sum (eight independent
+      // partial sums, so the add chain is 16 deep instead of 128).
+      float ps[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int key = key0 + col;
             const bool valid = full || (key < key_end && (!a.causal || key <= qpos));
             pf[i] = valid ? ex2_approx(fmaf(__uint_as_float(v[g * 8 + i]), a.scale_log2, -m_use)) : 0.f;
-            psum += pf[i];
+            ps[i] += pf[i];
           }
           uint4 packed;
           packed.x = pack2<T>(pf[0], pf[1]);
@@ -287,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&p_full[j & 1]);
+      const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l_run = l_run * alpha + psum;
       m_run = m_new;
       if (j > 0 && !correct(j - 1, alpha_prev)) { ok = false; break; }
@@ -355,7 +367,7 @@ int launch_tc(const void* q, const void* cache, int64_t cbs, int64_t css, int64_
     attr[dev & 63] = true;
   }
   PAArgs args{(int)S, (int)hq, (int)hk, causal, scale * 1.4426950408889634f, out, pos_start, cbo};
-  dim3 grid(ceil_div(S, kRows), (unsigned)hq, (unsigned)B);
+  dim3 grid((unsigned)hq, ceil_div(S, kRows), (unsigned)B);
   kern<<<grid, kThreads, L::kSmem, stream>>>(mq, mkv, args);
   HX_LAUNCH_CHECK("prefill_attn_tc_kernel");
   return HX_OK;
