@@ -9,14 +9,15 @@
 //   warp 0      TMA: the Q tile once, then K/V tiles of 128 keys straight out of the KV cache
 //               ([B, max_seq, 2, hkv, d], a 4D tensor map) into a 2-stage ring.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into a double-buffered TMEM score tile
-//               (M=128, N=128, K=d); O_j = P_j V_j into a double-buffered TMEM output tile
-//               (M=128, N=d, K=128, V read MN-major). S_{j+1} is issued before O_j, so QK^T
-//               overlaps the softmax.
-//   warps 2-5   softmax + epilogue: thread = query row. Two tcgen05.ld passes over the score
-//               row (max, then exp2/sum; tiles below the causal diagonal skip the mask), P
-//               written to a double-buffered shared-memory tile in the SW128 K-major layout the
-//               MMA reads; O_j is added to the register accumulator (online rescale) after the
-//               softmax of tile j+1, so that softmax runs while the tensor core computes O_j.
+//               (M=128, N=128, K=d); O += P_j V_j into one TMEM output tile (M=128, N=d,
+//               K=128, V read MN-major). S_{j+1} is issued before P_j V_j, so QK^T overlaps
+//               the softmax.
+//   warps 2-5   softmax + epilogue: thread = query row. The score row is read from TMEM once
+//               (tiles below the causal diagonal skip the mask), P written to a double-buffered
+//               shared-memory tile in the SW128 K-major layout the MMA reads. O never leaves
+//               TMEM until the epilogue: the reference max of a row only moves when a tile's
+//               max exceeds it by more than 2^8 (conditional rescaling, FlashAttention-4), and
+//               only then is O rescaled in place (tcgen05.ld / st), so P stays below 256.
 // Cache rows past the live range may hold stale bits; their scores are masked to -inf and
 // their V rows are zeroed in shared memory before P.V so 0 * stale never reaches the MMA.
 #include "common.cuh"
@@ -37,7 +38,7 @@ struct Lay {
   static constexpr int kPBytes = 2 * kChunkBytes;         // one [128 x 128 keys] P tile
   static constexpr int kBar = kP + 2 * kPBytes;           // P[2]
   static constexpr size_t kSmem = kBar + 256 + 1024;
-  static constexpr uint32_t kTmemCols = 512;  // S[2] (256) + O[2] (2 x d)
+  static constexpr uint32_t kTmemCols = 512;  // S[2] (256) + O (d), rounded to a power of 2
   static constexpr uint32_t kOCol = 256;
 };
 
@@ -63,8 +64,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* s_empty = bars + 7;   // [2]
   uint64_t* p_full = bars + 9;   // [2]
-  uint64_t* o_full = bars + 11;  // [2]
-  uint64_t* o_empty = bars + 13; // [2]
+  uint64_t* o_full = bars + 11;  // [2]: P_j V_j complete, committed to o_full[j & 1]
   uint64_t* drain = bars + 15;  // MMA completion barrier used on exit
   uint32_t* counters = reinterpret_cast<uint32_t*>(bars + 16);  // [0] kv issued [1] kv consumed [2] q consumed
   uint32_t* tmem_slot = counters + 3;
@@ -94,7 +94,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
     }
     mbar_init(drain, 1);
     counters[0] = counters[1] = counters[2] = 0;
@@ -160,7 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; ok && j < n_tiles; ++j) {
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) break;
-        if (!mbar_wait(&o_empty[j & 1], ((j >> 1) & 1) ^ 1)) break;
         tc_fence_after();
         const int st = j & 1;
         const uint32_t pa = smem_u32(sm + L::kP + (j & 1) * L::kPBytes);
@@ -170,9 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int key = kc * 64 + k * 16;
-            tc_mma_f16(tmem + L::kOCol + (j & 1) * D, sw128_kmajor_desc(pa + kc * kChunkBytes + k * 32),
+            tc_mma_f16(tmem + L::kOCol, sw128_kmajor_desc(pa + kc * kChunkBytes + k * 32),
                        sw128_mnmajor_desc(va + key * 128, kChunkBytes, 1024), idesc_o,
-                       (kc | k) ? 1u : 0u);
+                       (j | kc | k) ? 1u : 0u);
           }
         tc_commit(&o_full[j & 1]);
         tc_commit(&kv_empty[st]);
@@ -188,87 +186,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const int qpos = p0 + q0 + r;
-    float o_acc[D];
-#pragma unroll
-    for (int e = 0; e < D; ++e) o_acc[e] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    // m_ref: the row's reference max (log2 units) that P is taken against; l_run: sum of P.
+    float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
-    // O_j (the P.V of tile j) is added to the register accumulator after the softmax of tile
-    // j + 1, so that softmax overlaps the P.V MMA; alpha_prev is tile j's rescale factor.
-    float alpha_prev = 1.f;
-    auto correct = [&](int jj, float al) -> bool {
-      if (!mbar_wait_warp(&o_full[jj & 1], (jj >> 1) & 1)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + L::kOCol + (jj & 1) * D + c * 32, v);
-        tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * al + __uint_as_float(v[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&o_empty[jj & 1]);
-      return true;
-    };
+    // Ordering facts used below: S_j is issued after P_{j-2} V_{j-2}, and a tcgen05.commit
+    // covers every earlier MMA of the issuing thread, so once S_j is complete at most one P.V
+    // (P_{j-1} V_{j-1}) is still running, and each o_full[x] has at most one phase pending.
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int sb = j & 1;
       uint8_t* pbase = sm + L::kP + (j & 1) * L::kPBytes;
       if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
+      uint32_t v[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v[c]);
+      tc_wait_ld();
+      // The score tile is in registers: hand its TMEM buffer back for S_{j+2}.
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
       const int key0 = j * kRows;
       // Tiles wholly inside the live range and below the causal diagonal of every row of this
       // CTA need no mask (all but the last tile or two of a row block).
       const bool full = key0 + kRows <= key_end && (!a.causal || key0 + kRows - 1 <= p0 + q0);
-      // Pass 1: row max over valid keys (scale > 0, so max(s) * scale = max(s * scale)).
-      float tmax = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
-        tc_wait_ld();
-        if (full) {
-          // Tree of independent maxima (a 5-deep chain instead of 32).
-          float m8[8];
+      if (!full) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            m8[k] = fmaxf(fmaxf(__uint_as_float(v[k]), __uint_as_float(v[k + 8])),
-                          fmaxf(__uint_as_float(v[k + 16]), __uint_as_float(v[k + 24])));
-#pragma unroll
-          for (int k = 0; k < 4; ++k) m8[k] = fmaxf(m8[k], m8[k + 4]);
-          const float mx = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
-          tmax = fmaxf(tmax, mx * a.scale_log2);
-        } else {
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int key = key0 + c * 32 + i;
             const bool valid = key < key_end && (!a.causal || key <= qpos);
-            if (valid) tmax = fmaxf(tmax, __uint_as_float(v[i]) * a.scale_log2);
+            if (!valid) v[c][i] = 0xff800000u;  // -inf: exp2 gives 0
           }
+      }
+      // Row max: eight independent 16-deep chains, then a tree.
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(v[0][k]);
+#pragma unroll
+      for (int idx = 8; idx < 128; idx += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(v[idx >> 5][(idx & 31) + k]));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m8[k] = fmaxf(m8[k], m8[k + 4]);
+      // scale > 0, so max(s) * scale = max(s * scale); -inf stays -inf.
+      const float tmax = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])) * a.scale_log2;
+      // Conditional rescale. tcgen05.ld/st are warp-collective, so the warp decides together;
+      // every row of a rescaling warp moves its reference to its running max.
+      if (__any_sync(0xffffffffu, tmax > m_ref + 8.f)) {
+        const float m_new = fmaxf(m_ref, tmax);
+        const float alpha = m_ref == -INFINITY ? 0.f : ex2_approx(m_ref - m_new);
+        l_run *= alpha;
+        m_ref = m_new;
+        if (j > 0) {
+          // O holds P_0 V_0 .. P_{j-1} V_{j-1}; wait for the last of them, scale in place.
+          if (!mbar_wait_warp(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(lane_addr + L::kOCol + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(lane_addr + L::kOCol + c * 32, o);
+          }
+          tc_wait_st();
+          tc_fence_before();
         }
       }
-      const float m_new = fmaxf(m_run, tmax);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2_approx(m_run - m_use);
-      // Pass 2: probabilities -> P (swizzled K-major) and the row sum (eight independent
-      // partial sums, so the add chain is 16 deep instead of 128).
+      // m_ref is finite from the first tile on (key 0 is valid for every row).
+      const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+      // P = exp2(s * scale - m_ref) -> swizzled K-major smem, and the row sum (eight
+      // independent partial sums).
       float ps[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
-        tc_wait_ld();
 #pragma unroll
         for (int g = 0; g < 4; ++g) {  // 4 groups of 8 keys = 16 bytes of P
           float pf[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const int col = c * 32 + g * 8 + i;
-            const int key = key0 + col;
-            const bool valid = full || (key < key_end && (!a.causal || key <= qpos));
-            pf[i] = valid ? ex2_approx(fmaf(__uint_as_float(v[g * 8 + i]), a.scale_log2, -m_use)) : 0.f;
+            pf[i] = ex2_approx(fmaf(__uint_as_float(v[c][g * 8 + i]), a.scale_log2, -mu));
             ps[i] += pf[i];
           }
           uint4 packed;
@@ -282,8 +282,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(dst) = packed;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
       // Last tile: zero V rows past the live keys (their cache rows may be stale).
       if (j == n_tiles - 1) {
         const int valid_rows = key_end - key0;
@@ -298,22 +296,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&p_full[j & 1]);
-      const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      l_run = l_run * alpha + psum;
-      m_run = m_new;
-      if (j > 0 && !correct(j - 1, alpha_prev)) { ok = false; break; }
-      alpha_prev = alpha;
+      l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
     }
-    if (ok && n_tiles > 0 && !correct(n_tiles - 1, alpha_prev)) ok = false;
-    if (ok && r < nq) {
+    // Epilogue: the last P.V also completes every earlier one.
+    const int jl = n_tiles - 1;
+    if (ok && n_tiles > 0 && !mbar_wait_warp(&o_full[jl & 1], (jl >> 1) & 1)) ok = false;
+    if (ok && n_tiles > 0) {
+      tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       T* orow = reinterpret_cast<T*>(a.out) + (((int64_t)b * S + q0 + r) * a.n_heads + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(lane_addr + L::kOCol + c * 32, o);
+        tc_wait_ld();
+        if (r < nq) {
 #pragma unroll
-      for (int e = 0; e < D; e += 8) {
-        T pk[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) pk[i] = DT<T>::from_f(o_acc[e + i] * inv);
-        *reinterpret_cast<uint4*>(orow + e) = *reinterpret_cast<uint4*>(pk);
+          for (int e = 0; e < 32; e += 8) {
+            uint4 pk;
+            pk.x = pack2<T>(__uint_as_float(o[e + 0]) * inv, __uint_as_float(o[e + 1]) * inv);
+            pk.y = pack2<T>(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+            pk.z = pack2<T>(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+            pk.w = pack2<T>(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
+          }
+        }
       }
     }
   }

@@ -192,6 +192,26 @@ def test_prefill_attention(ops, dtype, hq, hk, d, S):
     torch.testing.assert_close(out.float(), ref.float(), rtol=tol, atol=tol)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_attention_growing_scores(ops, d):
+    """Scores that grow along the keys by far more than 2^8 per tile, so the tensor-core
+    kernel must rescale its TMEM output several times per row; plus a long multi-block case
+    with a start offset."""
+    dt, hq, hk = torch.bfloat16, 4, 2
+    g = torch.Generator().manual_seed(d)
+    for B, S, start in ((1, 520, 0), (2, 300, 37)):
+        cap = start + S + 3
+        q = (torch.randn(B, S, hq, d, generator=g) * 2).to(dt)
+        cache = torch.randn(B, cap, 2, hk, d, generator=g)
+        ramp = 1 + 6 * torch.arange(cap, dtype=torch.float32) / cap
+        cache[:, :, 0] *= ramp.view(1, cap, 1, 1)
+        cache = cache.to(dt)
+        starts = torch.full((B,), start, dtype=torch.int32)
+        out = ops.prefill_attention(q.cuda(), cache.cuda(), starts.cuda(), hk, d ** -0.5).cpu()
+        ref = flash_attention(q, cache[:, :start + S], True, d ** -0.5)
+        torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
 def test_prefill_attention_offsets_and_noncausal(ops):
     dt, hq, hk, d = torch.bfloat16, 8, 2, 64
     g = torch.Generator().manual_seed(11)
