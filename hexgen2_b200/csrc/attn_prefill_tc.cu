@@ -6,15 +6,22 @@
 // accumulation, bottom-right causal alignment (or no mask when causal == 0).
 //
 // One CTA = 128 queries of one head (f16/bf16, head_dim 64 or 128). Warp roles:
-//   warp 0      TMA: the Q tile once, then K/V tiles of 128 keys straight out of the KV cache
-//               ([B, max_seq, 2, hkv, d], a 4D tensor map) into a 2-stage ring.
+//   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys straight out of the KV
+//               cache ([B, max_seq, 2, hkv, d], a 4D tensor map) into separate 2-stage K and V
+//               rings, in the order the MMAs consume them (K0, K1, V0, K2, V1, ...). A K stage
+//               is free as soon as its QK^T completes, so K_{j+2} streams in while tile j's
+//               softmax and P.V still hold V_j.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into a double-buffered TMEM score tile
 //               (M=128, N=128, K=d); O += P_j V_j into one TMEM output tile (M=128, N=d,
 //               K=128, V read MN-major). S_{j+1} is issued before P_j V_j, so QK^T overlaps
 //               the softmax.
-//   warps 2-5   softmax + epilogue: thread = query row. The score row is read from TMEM once
-//               (tiles below the causal diagonal skip the mask), P written to a double-buffered
-//               shared-memory tile in the SW128 K-major layout the MMA reads. O never leaves
+//   warps 2-9   softmax + epilogue: two threads per query row, one in each of two
+//               warpgroups, each owning 64 of the tile's 128 key columns and half of the O
+//               columns. The score half-row is read from TMEM once (tiles below the causal
+//               diagonal skip the mask); the pair exchanges its partial row max through shared
+//               memory under a 64-thread named barrier; P is computed into registers and
+//               then stored, once the previous P.V has finished reading it, into a shared-memory
+//               tile in the SW128 K-major layout the MMA reads. O never leaves
 //               TMEM until the epilogue: the reference max of a row only moves when a tile's
 //               max exceeds it by more than 2^8 (conditional rescaling, FlashAttention-4), and
 //               only then is O rescaled in place (tcgen05.ld / st), so P stays below 256.
@@ -26,17 +33,20 @@ namespace {
 
 constexpr int kRows = 128;       // queries per CTA, keys per tile
 constexpr int kChunkBytes = kRows * 128;  // one [128 rows x 64 elements] swizzled chunk
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;    // TMA warp, MMA warp, 2 softmax warpgroups
 
 template <int D>
 struct Lay {
   static constexpr int kChunks = D / 64;
   static constexpr int kQ = 0;
-  static constexpr int kK0 = kChunks * kChunkBytes;
-  static constexpr int kKV = 2 * kChunks * kChunkBytes;  // K + V of one stage
-  static constexpr int kP = kK0 + 2 * kKV;
+  static constexpr int kTile = kChunks * kChunkBytes;    // one [128 keys x d] K or V tile
+  static constexpr int kK0 = kTile;                       // K ring [2]
+  static constexpr int kV0 = kK0 + 2 * kTile;             // V ring [2]
+  static constexpr int kP = kV0 + 2 * kTile;
   static constexpr int kPBytes = 2 * kChunkBytes;         // one [128 x 128 keys] P tile
-  static constexpr int kBar = kP + 2 * kPBytes;           // P[2]
+  static constexpr int kRed = kP + kPBytes;               // one P tile
+  // Max exchange: float [2 tiles][2 halves][128 rows]; the epilogue reuses it for row sums.
+  static constexpr int kBar = kRed + 2 * 2 * kRows * 4;
   static constexpr size_t kSmem = kBar + 256 + 1024;
   static constexpr uint32_t kTmemCols = 512;  // S[2] (256) + O (d), rounded to a power of 2
   static constexpr uint32_t kOCol = 256;
@@ -59,15 +69,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 9;   // [2] (by tile parity; one P tile)
   uint64_t* o_full = bars + 11;  // [2]: P_j V_j complete, committed to o_full[j & 1]
+  uint64_t* v_full = bars + 13;   // [2]
   uint64_t* drain = bars + 15;  // MMA completion barrier used on exit
-  uint32_t* counters = reinterpret_cast<uint32_t*>(bars + 16);  // [0] kv issued [1] kv consumed [2] q consumed
-  uint32_t* tmem_slot = counters + 3;
+  uint64_t* v_empty = bars + 16;  // [2]
+  // [0] K issued [1] K consumed [2] q consumed [3] V issued [4] V consumed
+  uint32_t* counters = reinterpret_cast<uint32_t*>(bars + 18);
+  uint32_t* tmem_slot = counters + 5;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Heads vary fastest and query blocks run last-to-first, so under a causal mask the CTAs with
@@ -86,17 +99,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmKV);
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_empty[i], 256);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
-    counters[0] = counters[1] = counters[2] = 0;
+    counters[0] = counters[1] = counters[2] = counters[3] = counters[4] = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -114,21 +129,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < L::kChunks; ++c)
         tma_load_3d(sm + L::kQ + c * kChunkBytes, &tmQ, q_full, c * 64, h, b * S + q0);
       const int bb = (int)(a.cache_batch_offset + b);
-      uint32_t issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) break;
-        mbar_arrive_expect_tx(&kv_full[st], L::kKV);
-        uint8_t* kb = sm + L::kK0 + st * L::kKV;
-        uint8_t* vb = kb + L::kChunks * kChunkBytes;
-        for (int c = 0; c < L::kChunks; ++c) {
-          tma_load_4d(kb + c * kChunkBytes, &tmKV, &kv_full[st], c * 64, hk, j * kRows, bb);
-          tma_load_4d(vb + c * kChunkBytes, &tmKV, &kv_full[st], c * 64, a.n_heads_kv + hk,
-                      j * kRows, bb);
+      uint32_t k_issued = 0, v_issued = 0;
+      // Step i loads K_i, then V_{i-1}: the MMA thread's order is S_0, S_1, PV_0, S_2, PV_1, ...
+      for (int i = 0; i <= n_tiles; ++i) {
+        if (i < n_tiles) {
+          const int st = i & 1;
+          if (!mbar_wait(&k_empty[st], ((i >> 1) & 1) ^ 1)) break;
+          mbar_arrive_expect_tx(&k_full[st], L::kTile);
+          uint8_t* kb = sm + L::kK0 + st * L::kTile;
+          for (int c = 0; c < L::kChunks; ++c)
+            tma_load_4d(kb + c * kChunkBytes, &tmKV, &k_full[st], c * 64, hk, i * kRows, bb);
+          ++k_issued;
         }
-        ++issued;
+        if (i >= 1) {
+          const int t = i - 1, st = t & 1;
+          if (!mbar_wait(&v_empty[st], ((t >> 1) & 1) ^ 1)) break;
+          mbar_arrive_expect_tx(&v_full[st], L::kTile);
+          uint8_t* vb = sm + L::kV0 + st * L::kTile;
+          for (int c = 0; c < L::kChunks; ++c)
+            tma_load_4d(vb + c * kChunkBytes, &tmKV, &v_full[st], c * 64, a.n_heads_kv + hk,
+                        t * kRows, bb);
+          ++v_issued;
+        }
       }
-      counters[0] = issued;
+      counters[0] = k_issued;
+      counters[3] = v_issued;
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -136,15 +161,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_o = make_idesc_f16<T>(128, D, 0, 1);
       bool ok = mbar_wait(q_full, 0);
       counters[2] = ok ? 1u : 0u;
-      uint32_t consumed = 0;
+      uint32_t k_consumed = 0, v_consumed = 0;
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1, sb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
-        ++consumed;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        ++k_consumed;
         if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(sm + L::kQ);
-        const uint32_t ka = smem_u32(sm + L::kK0 + st * L::kKV);
+        const uint32_t ka = smem_u32(sm + L::kK0 + st * L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c)
 #pragma unroll
@@ -153,16 +178,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                        sw128_kmajor_desc(ka + c * kChunkBytes + k * 32), idesc_s,
                        (c | k) ? 1u : 0u);
         tc_commit(&s_full[sb]);
+        tc_commit(&k_empty[st]);
         return true;
       };
       if (ok && n_tiles > 0) ok = issue_s(0);
       for (int j = 0; ok && j < n_tiles; ++j) {
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        const int st = j & 1;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1)) break;
+        ++v_consumed;
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) break;
         tc_fence_after();
-        const int st = j & 1;
-        const uint32_t pa = smem_u32(sm + L::kP + (j & 1) * L::kPBytes);
-        const uint32_t va = smem_u32(sm + L::kK0 + st * L::kKV + L::kChunks * kChunkBytes);
+        const uint32_t pa = smem_u32(sm + L::kP);
+        const uint32_t va = smem_u32(sm + L::kV0 + st * L::kTile);
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc)
 #pragma unroll
@@ -173,63 +201,81 @@ __global__ void __launch_bounds__(kThreads, 1)
                        (j | kc | k) ? 1u : 0u);
           }
         tc_commit(&o_full[j & 1]);
-        tc_commit(&kv_empty[st]);
+        tc_commit(&v_empty[st]);
       }
       // No MMA of this CTA may still be running when TMEM is freed.
       tc_commit(drain);
       mbar_wait(drain, 0);
-      counters[1] = consumed;
+      counters[1] = k_consumed;
+      counters[4] = v_consumed;
     }
   } else {
-    // Softmax / epilogue warps: row r of the tile, TMEM lane quarter = warp % 4.
-    const int quarter = warp & 3;
+    // Softmax / epilogue warps: row r of the tile (TMEM lane quarter = warp % 4); warpgroup
+    // `half` owns key columns [64 half, 64 half + 64) and O columns [half D/2, half D/2 + D/2).
+    // The two warps of a row quarter meet at named barrier 1 + quarter (64 threads).
+    constexpr int kOHalf = D / 2;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const int qpos = p0 + q0 + r;
-    // m_ref: the row's reference max (log2 units) that P is taken against; l_run: sum of P.
+    float* red = reinterpret_cast<float*>(sm + L::kRed);  // [2][2][128], then [2][128]
+    const int bar_id = 1 + quarter;
+    // m_ref: the row's reference max (log2 units) that P is taken against; l_run: this half's
+    // sum of P.
     float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
     // Ordering facts used below: S_j is issued after P_{j-2} V_{j-2}, and a tcgen05.commit
     // covers every earlier MMA of the issuing thread, so once S_j is complete at most one P.V
     // (P_{j-1} V_{j-1}) is still running, and each o_full[x] has at most one phase pending.
-    for (int j = 0; ok && j < n_tiles; ++j) {
+    for (int j = 0; j < n_tiles; ++j) {
       const int sb = j & 1;
-      uint8_t* pbase = sm + L::kP + (j & 1) * L::kPBytes;
-      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t v[4][32];
+      const bool got = ok && mbar_wait_warp(&s_full[sb], (j >> 1) & 1);
+      uint32_t v[2][32];
+      float hmax = -INFINITY;
+      const int key0 = j * kRows + half * 64;
+      if (got) {
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v[c]);
-      tc_wait_ld();
-      // The score tile is in registers: hand its TMEM buffer back for S_{j+2}.
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
-      const int key0 = j * kRows;
-      // Tiles wholly inside the live range and below the causal diagonal of every row of this
-      // CTA need no mask (all but the last tile or two of a row block).
-      const bool full = key0 + kRows <= key_end && (!a.causal || key0 + kRows - 1 <= p0 + q0);
-      if (!full) {
+        for (int c = 0; c < 2; ++c) tmem_ld_32x32b_x32(lane_addr + sb * 128 + half * 64 + c * 32, v[c]);
+        tc_wait_ld();
+        // The score tile is in registers: hand its TMEM buffer back for S_{j+2}.
+        tc_fence_before();
+        mbar_arrive(&s_empty[sb]);
+        // Tiles wholly inside the live range and below the causal diagonal of every row of
+        // this CTA need no mask (all but the last tile or two of a row block).
+        const bool full = j * kRows + kRows <= key_end && (!a.causal || j * kRows + kRows - 1 <= p0 + q0);
+        if (!full) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = key0 + c * 32 + i;
-            const bool valid = key < key_end && (!a.causal || key <= qpos);
-            if (!valid) v[c][i] = 0xff800000u;  // -inf: exp2 gives 0
-          }
+            for (int i = 0; i < 32; ++i) {
+              const int key = key0 + c * 32 + i;
+              const bool valid = key < key_end && (!a.causal || key <= qpos);
+              if (!valid) v[c][i] = 0xff800000u;  // -inf: exp2 gives 0
+            }
+        }
+        // Half-row max: eight independent 8-deep chains, then a tree.
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(v[0][k]);
+#pragma unroll
+        for (int idx = 8; idx < 64; idx += 8)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(v[idx >> 5][(idx & 31) + k]));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) m8[k] = fmaxf(m8[k], m8[k + 4]);
+        hmax = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
       }
-      // Row max: eight independent 16-deep chains, then a tree.
-      float m8[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(v[0][k]);
-#pragma unroll
-      for (int idx = 8; idx < 128; idx += 8)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(v[idx >> 5][(idx & 31) + k]));
-#pragma unroll
-      for (int k = 0; k < 4; ++k) m8[k] = fmaxf(m8[k], m8[k + 4]);
-      // scale > 0, so max(s) * scale = max(s * scale); -inf stays -inf.
-      const float tmax = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])) * a.scale_log2;
+      // Exchange with the partner half. Slot j & 1: a slot is rewritten two tiles later, after
+      // the partner has passed the barrier of the tile in between, i.e. after it read this
+      // value. The barrier also carries the pair's common go / abort decision.
+      red[((j & 1) * 2 + half) * kRows + r] = hmax;
+      ok = named_bar_and(bar_id, 64, got);
+      if (!ok) break;
+      const float pmax = red[((j & 1) * 2 + (half ^ 1)) * kRows + r];
+      // scale > 0, so max(s) * scale = max(s * scale); -inf stays -inf. fmaxf is commutative,
+      // so both halves of a row hold the same value and take the same decisions below.
+      const float tmax = fmaxf(hmax, pmax) * a.scale_log2;
       // Conditional rescale. tcgen05.ld/st are warp-collective, so the warp decides together;
       // every row of a rescaling warp moves its reference to its running max.
       if (__any_sync(0xffffffffu, tmax > m_ref + 8.f)) {
@@ -238,59 +284,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         l_run *= alpha;
         m_ref = m_new;
         if (j > 0) {
-          // O holds P_0 V_0 .. P_{j-1} V_{j-1}; wait for the last of them, scale in place.
-          if (!mbar_wait_warp(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1)) { ok = false; break; }
-          tc_fence_after();
+          // O holds P_0 V_0 .. P_{j-1} V_{j-1}; wait for the last of them, scale this half in
+          // place. A timed-out wait skips the scaling (the result is then discarded).
+          if (!mbar_wait_warp(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+            ok = false;
+          } else {
+            tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld_32x32b_x32(lane_addr + L::kOCol + c * 32, o);
-            tc_wait_ld();
+            for (int c = 0; c < kOHalf / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld_32x32b_x32(lane_addr + L::kOCol + half * kOHalf + c * 32, o);
+              tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_32x32b_x32(lane_addr + L::kOCol + c * 32, o);
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st_32x32b_x32(lane_addr + L::kOCol + half * kOHalf + c * 32, o);
+            }
+            tc_wait_st();
+            tc_fence_before();
           }
-          tc_wait_st();
-          tc_fence_before();
         }
       }
       // m_ref is finite from the first tile on (key 0 is valid for every row).
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      // P = exp2(s * scale - m_ref) -> swizzled K-major smem, and the row sum (eight
+      // P = exp2(s * scale - m_ref) into registers, and this half's row sum (eight
       // independent partial sums).
       float ps[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int u = 0; u < 8; ++u) {  // 8 groups of 8 keys = 16 bytes of P each
+        float pf[8];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {  // 4 groups of 8 keys = 16 bytes of P
-          float pf[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            pf[i] = ex2_approx(fmaf(__uint_as_float(v[c][g * 8 + i]), a.scale_log2, -mu));
-            ps[i] += pf[i];
-          }
-          uint4 packed;
-          packed.x = pack2<T>(pf[0], pf[1]);
-          packed.y = pack2<T>(pf[2], pf[3]);
-          packed.z = pack2<T>(pf[4], pf[5]);
-          packed.w = pack2<T>(pf[6], pf[7]);
-          const int col0 = c * 32 + g * 8;
-          const int kc = col0 >> 6, unit = (col0 & 63) >> 3;
-          uint8_t* dst = pbase + kc * kChunkBytes + r * 128 + ((unit ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = packed;
+        for (int i = 0; i < 8; ++i) {
+          pf[i] = ex2_approx(fmaf(__uint_as_float(v[u >> 2][(u & 3) * 8 + i]), a.scale_log2, -mu));
+          ps[i] += pf[i];
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pk[u * 4 + i] = pack2<T>(pf[2 * i], pf[2 * i + 1]);
       }
-      // Last tile: zero V rows past the live keys (their cache rows may be stale).
-      if (j == n_tiles - 1) {
-        const int valid_rows = key_end - key0;
-        if (r >= valid_rows) {
-          uint8_t* vrow = sm + L::kK0 + (j & 1) * L::kKV + L::kChunks * kChunkBytes + r * 128;
+      // The P tile is single-buffered: P_{j-1} V_{j-1} must be done reading it. S_j complete
+      // implies P_{j-2} V_{j-2} complete, so o_full[(j-1) & 1] has one phase pending at most.
+      if (j > 0 && !mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1)) ok = false;
+      // Chunk `half` of the swizzled K-major P tile.
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        uint8_t* dst = sm + L::kP + half * kChunkBytes + r * 128 + ((u ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[u * 4], pk[u * 4 + 1], pk[u * 4 + 2], pk[u * 4 + 3]);
+      }
+      // Last tile: zero V rows past the live keys (their cache rows may be stale); each half
+      // clears every other 16-byte unit of the row.
+      // V_j lands on its own barrier: wait for it (V_{j-2}, the barrier's previous phase, has
+      // been consumed by P_{j-2} V_{j-2}, so the parity is unambiguous).
+      if (j == n_tiles - 1 && r >= key_end - j * kRows) {
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1)) {
+          ok = false;
+        } else {
+          uint8_t* vrow = sm + L::kV0 + (j & 1) * L::kTile + r * 128;
 #pragma unroll
           for (int c = 0; c < L::kChunks; ++c)
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = half; u < 8; u += 2)
               *reinterpret_cast<uint4*>(vrow + c * kChunkBytes + u * 16) = make_uint4(0, 0, 0, 0);
         }
       }
@@ -298,17 +352,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&p_full[j & 1]);
       l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
     }
-    // Epilogue: the last P.V also completes every earlier one.
+    // Epilogue: the last P.V also completes every earlier one. The pair adds its row sums.
     const int jl = n_tiles - 1;
     if (ok && n_tiles > 0 && !mbar_wait_warp(&o_full[jl & 1], (jl >> 1) & 1)) ok = false;
+    ok = named_bar_and(bar_id, 64, ok);
     if (ok && n_tiles > 0) {
+      // (The partner read its last max before arriving at the barrier above.)
+      red[half * kRows + r] = l_run;
+      named_bar_sync(bar_id, 64);
+      const float l_tot = l_run + red[(half ^ 1) * kRows + r];
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* orow = reinterpret_cast<T*>(a.out) + (((int64_t)b * S + q0 + r) * a.n_heads + h) * D;
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      T* orow = reinterpret_cast<T*>(a.out) + (((int64_t)b * S + q0 + r) * a.n_heads + h) * D + half * kOHalf;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < kOHalf / 32; ++c) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lane_addr + L::kOCol + c * 32, o);
+        tmem_ld_32x32b_x32(lane_addr + L::kOCol + half * kOHalf + c * 32, o);
         tc_wait_ld();
         if (r < nq) {
 #pragma unroll
@@ -331,7 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     if (!counters[2]) mbar_wait(q_full, 0);
     for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait(&kv_full[i & 1], (i >> 1) & 1)) break;
+      if (!mbar_wait(&k_full[i & 1], (i >> 1) & 1)) break;
+    for (uint32_t i = counters[4]; i < counters[3]; ++i)
+      if (!mbar_wait(&v_full[i & 1], (i >> 1) & 1)) break;
   }
   __syncthreads();
   tc_fence_after();
