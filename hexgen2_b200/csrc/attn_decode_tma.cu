@@ -232,17 +232,36 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
   bool ok = true;
   // Every consumer warp walks the same piece / tile / barrier sequence even after a failed
   // (timed-out) wait, only skipping the work, so no warp is left waiting at a named barrier.
+  // The query and live length of the next piece are loaded while the current one runs, so a
+  // piece boundary costs no global-memory round trip.
+  constexpr int kQPer = (G * D + 32 * kConsumers - 1) / (32 * kConsumers);
   PieceWalker walker(pre, hkv, a.batch, u0, u1);
-  Piece pc;
-  while (walker.next(pc)) {
+  Piece pc, pn;
+  T qn[kQPer];
+  int len_n = 0;
+  auto prefetch = [&](const Piece& x) {
+#pragma unroll
+    for (int i = 0; i < kQPer; ++i) {
+      const int idx = ct + i * 32 * kConsumers;
+      if (idx < G * D)
+        qn[i] = reinterpret_cast<const T*>(a.q)[((int64_t)x.b * a.n_heads + x.hk * G) * D + idx];
+    }
+    len_n = live_len(a, x.b);
+  };
+  bool have = walker.next(pc);
+  if (have) prefetch(pc);
+  while (have) {
     const int b = pc.b, hk = pc.hk;
-    const int len = live_len(a, b);
+    const int len = len_n;
+#pragma unroll
+    for (int i = 0; i < kQPer; ++i) {
+      const int idx = ct + i * 32 * kConsumers;
+      if (idx < G * D) q_s[idx] = DT<T>::to_f(qn[i]) * a.scale_log2;
+    }
+    const bool have_next = walker.next(pn);
+    if (have_next) prefetch(pn);
     const int start = pc.t_lo * kTileKeys;
     const int end = min(pc.t_hi * kTileKeys, len);
-    for (int idx = ct; idx < G * D; idx += 32 * kConsumers) {
-      const int g = idx / D, e = idx % D;
-      q_s[g * D + e] = DT<T>::to_f(reinterpret_cast<const T*>(a.q)[((int64_t)b * a.n_heads + hk * G + g) * D + e]) * a.scale_log2;
-    }
     named_barrier_consumers();
     float m[G], l[G], o[G][kDims];
 #pragma unroll
@@ -327,8 +346,10 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
           for (int i = 0; i < 2; ++i) vf[i] = DT<T>::to_f(ve[i]);
         }
       };
-      if (n_valid == 32) {
-        // Full 32-key slice: unrolled, two accumulator sets to halve the FMA chain.
+      {
+        // 32-key slice, unrolled, two accumulator sets to halve the FMA chain. Keys past the
+        // live range (the last tile of a run) are skipped by predication: their V rows may hold
+        // stale bytes, so they must not enter an FMA even with p = 0.
         float o2[G][kDims];
 #pragma unroll
         for (int g = 0; g < G; ++g)
@@ -339,14 +360,15 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
           float v0[kDims], v1[kDims];
           load_v(k, v0);
           load_v(k + 1, v1);
+          const bool use0 = k < n_valid, use1 = k + 1 < n_valid;
 #pragma unroll
           for (int g = 0; g < G; ++g) {
             const float p0 = __shfl_sync(0xffffffffu, pr[g], k);
             const float p1 = __shfl_sync(0xffffffffu, pr[g], k + 1);
 #pragma unroll
             for (int i = 0; i < kDims; ++i) {
-              o[g][i] = fmaf(p0, v0[i], o[g][i]);
-              o2[g][i] = fmaf(p1, v1[i], o2[g][i]);
+              if (use0) o[g][i] = fmaf(p0, v0[i], o[g][i]);
+              if (use1) o2[g][i] = fmaf(p1, v1[i], o2[g][i]);
             }
           }
         }
@@ -354,17 +376,6 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
         for (int g = 0; g < G; ++g)
 #pragma unroll
           for (int i = 0; i < kDims; ++i) o[g][i] += o2[g][i];
-      } else {
-        for (int k = 0; k < n_valid; ++k) {
-          float vf[kDims];
-          load_v(k, vf);
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float pk = __shfl_sync(0xffffffffu, pr[g], k);
-#pragma unroll
-            for (int i = 0; i < kDims; ++i) o[g][i] = fmaf(pk, vf[i], o[g][i]);
-          }
-        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
@@ -412,6 +423,8 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
       }
     }
     named_barrier_consumers();
+    pc = pn;
+    have = have_next;
   }
 }
 
