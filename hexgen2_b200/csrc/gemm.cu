@@ -815,6 +815,241 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Prefill GEMM on CTA pairs (tcgen05 cta_group::2): one 256 x 256 output tile per pair of SMs.
+//   The pair's MMA computes D[256 x 256] += A[256 x 16] B[256 x 16]^T per instruction; each CTA
+//   holds its own 128 rows of A and its own 128 rows (output columns) of B in shared memory and
+//   receives its 128 rows x 256 columns of D in its own TMEM. Per SM and k-block that is 32 KB
+//   written by TMA and read by the tensor core for 4.2 MFLOP, half the shared-memory traffic of
+//   a single-SM 128 x 256 tile, which is what bounds the single-SM kernel.
+//   Roles per CTA: warp 0 TMA producer (both CTAs), warp 1 MMA issuer (even CTA only) and TMEM
+//   owner, warps 2-5 epilogue (both CTAs).
+//   Signals: the even CTA arms its stage barrier with both CTAs' bytes and both CTAs' TMA loads
+//   complete on it; the MMA commits to the even CTA's barriers, whose observers relay them to
+//   the odd CTA with a remote mbarrier arrive (stage free: the even producer; accumulator full:
+//   an even epilogue thread); both epilogues release an accumulator on the even CTA's barrier.
+//   Persistent over (row pair, column tile) work items; two TMEM accumulators so the epilogue
+//   of one item overlaps the main loop of the next.
+// ------------------------------------------------------------------------------------------
+constexpr int kPairStages = 7;
+constexpr int kPairTileBytes = 128 * BK * 2;                 // 128 rows x 64 k of A or of B
+constexpr int kPairStageBytes = 2 * kPairTileBytes;
+constexpr size_t kPairSmem = (size_t)kPairStages * kPairStageBytes + 1024 + 512;
+
+HX_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+HX_DEVICE void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+HX_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+HX_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D(tmem, both CTAs) (+)= A * B^T over the pair; issued by the even CTA with its own smem
+// descriptors (the odd CTA's operands sit at the same offsets). No output lanes are disabled.
+HX_DEVICE void tc_mma_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                           uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+      ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate), "r"(z)
+      : "memory");
+}
+// Arrive on a barrier of this CTA once all earlier pair MMAs issued by this thread complete.
+HX_DEVICE void tc_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// Tiled 2D TMA load into this CTA's shared memory whose completion is counted on an mbarrier
+// that may live in the peer CTA of the pair (cluster address).
+HX_DEVICE void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+// Arrive on an mbarrier given by cluster address (this CTA's or the peer's), with the default
+// CTA-scope release: the signals relayed with it carry no data of the arriving thread (what they
+// order is the MMA's completion, established by tcgen05.commit and the tcgen05 fences), and a
+// cluster-scope release would stall the thread until its earlier global stores are acknowledged.
+HX_DEVICE void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+  constexpr int BNP = 256;  // output columns per pair tile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + kPairStages * kPairTileBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* counters = reinterpret_cast<uint32_t*>(drain + 1);  // [0] loads issued, [1] consumed
+  uint32_t* tmem_slot = counters + 2;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0 = even CTA (issues the MMAs), 1 = odd
+  const bool even = rank == 0;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int pm_tiles = (a.M + 2 * BM - 1) / (2 * BM);
+  const int total = pm_tiles * a.n_tiles;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);  // one arrive per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    counters[0] = counters[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BNP);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised before any remote arrive or load
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // A (activations) and the epilogue inputs come from earlier kernels
+
+  // Cluster addresses of the even CTA's barriers / the odd CTA's relay targets.
+  const uint32_t full_even = dsmem_map(smem_u32(full), 0);
+  const uint32_t tempty_even = dsmem_map(smem_u32(tempty), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t empty_odd = dsmem_map(smem_u32(empty), 1);
+      int stage = 0;
+      uint32_t phase = 0, issued = 0;
+      for (int t = pair; t < total; t += n_pairs) {
+        const int pm = t % pm_tiles, nb = t / pm_tiles;
+        const int row_a = pm * 2 * BM + (int)rank * BM;
+        const int row_b = nb * BNP + (int)rank * BM;
+        for (int kb = 0; kb < a.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) goto producer_done;
+          // The even CTA saw the MMAs release this stage: pass it on to the odd CTA (from the
+          // second round on; the first round of every stage starts free in both CTAs).
+          if (even && issued >= (uint32_t)kPairStages) mbar_arrive_remote(empty_odd + stage * 8);
+          if (even) mbar_arrive_expect_tx(&full[stage], kPairStageBytes * 2);
+          tma_load_2d_pair(smA + stage * kPairTileBytes, &tmA, full_even + stage * 8, kb * BK, row_a);
+          tma_load_2d_pair(smB + stage * kPairTileBytes, &tmB, full_even + stage * 8, kb * BK, row_b);
+          ++issued;
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:
+      counters[0] = issued;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && even) {
+      constexpr uint32_t idesc = make_idesc_f16<T>(2 * BM, BNP);
+      int stage = 0;
+      uint32_t phase = 0, consumed = 0;
+      int local = 0;
+      for (int t = pair; t < total; t += n_pairs, ++local) {
+        const int acc = local & 1;
+        if (!mbar_wait(&tempty[acc], ((local >> 1) & 1) ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BNP;
+        for (int kb = 0; kb < a.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) goto mma_done;
+          ++consumed;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + stage * kPairTileBytes);
+          const uint32_t b_addr = smem_u32(smB + stage * kPairTileBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma_pair(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
+                        idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[stage]);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        tc_commit_pair(&tfull[acc]);
+      }
+    mma_done:
+      tc_commit_pair(drain);
+      mbar_wait(drain, 0);
+      counters[1] = consumed;
+    }
+  } else {
+    // Epilogue warps 2..5 of both CTAs: TMEM lane quarter = warp % 4, this CTA's 128 rows.
+    const int quarter = warp & 3;
+    const uint32_t tfull_odd = dsmem_map(smem_u32(tfull), 1);
+    int local = 0;
+    for (int t = pair; t < total; t += n_pairs, ++local) {
+      const int pm = t % pm_tiles, nb = t / pm_tiles;
+      const int acc = local & 1;
+      if (!mbar_wait_warp(&tfull[acc], (local >> 1) & 1)) break;
+      // Relay "accumulator ready" to the odd CTA (its MMAs completed with the same commit).
+      if (even && warp == 2 && lane == 0) mbar_arrive_remote(tfull_odd + acc * 8);
+      tc_fence_after();
+      const int m = pm * 2 * BM + (int)rank * BM + quarter * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BNP / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BNP + c * 32, r);
+        tc_wait_ld();
+        const int n0 = nb * BNP + c * 32;
+        if (n0 >= a.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        epilogue_store<T, EPI>(a, m, n0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_even + acc * 8);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // After an aborted wait, let issued-but-unconsumed loads land (bounded) before shared
+  // memory goes away; they all complete on the even CTA's barriers.
+  if (threadIdx.x == 0 && even) {
+    for (uint32_t i = counters[1]; i < counters[0]; ++i)
+      if (!mbar_wait(&full[i % kPairStages], (i / kPairStages) & 1)) break;
+  }
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal or read it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, 2 * BNP);
+}
+
 // ---------------------------------------------------------------------------------------
 // Host side: tensor maps, tile selection, launch.
 // ---------------------------------------------------------------------------------------
@@ -833,7 +1068,11 @@ int device_sms() { return device_sm_count(); }
 struct Plan {
   int bn, m_tiles, n_tiles, k_splits, kb_per_split, k_blocks;
   bool swap;    // decode-shaped: operands swapped, split-K inside a cluster (chosen at launch)
+  bool pair;    // 256 x 256 tiles on CTA pairs (gemm_pair_kernel)
 };
+
+// Work items of the CTA-pair kernel: (256-row block, 256-column block).
+int64_t pair_items(int64_t M, int64_t N) { return (int64_t)ceil_div(M, 2 * BM) * ceil_div(N, 256); }
 
 // Tile / split selection.
 //  * Decode-shaped (M <= 64): operands swapped (128 weight rows per tile, N = batch rounded up
@@ -845,8 +1084,15 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
   Plan p;
   p.k_blocks = ceil_div(K, BK);
   p.swap = M <= 64;
+  // CTA pairs when there are rows for both halves and enough 256 x 256 items to occupy ~80%
+  // of the pairs in one wave; otherwise single-SM tiles with a K split.
+  p.pair = !p.swap && M > BM && N >= 256 && pair_items(M, N) * 5 >= (int64_t)(sms / 2) * 4;
   int splits = 1;
-  if (p.swap) {
+  if (p.pair) {
+    p.bn = 256;
+    p.m_tiles = ceil_div(M, BM);
+    p.n_tiles = ceil_div(N, 256);
+  } else if (p.swap) {
     p.bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     p.m_tiles = ceil_div(N, BM);
     p.n_tiles = 1;
@@ -870,7 +1116,7 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
 }
 
 size_t plan_workspace(const Plan& p, int64_t M, int64_t N) {
-  if (p.swap) return 0;
+  if (p.swap || p.pair) return 0;
   return p.k_splits > 1 ? (size_t)p.k_splits * M * N * sizeof(float) : 0;
 }
 
@@ -941,6 +1187,30 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
 }
 
 template <typename T, int EPI>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+                cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<T, EPI>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    int s = hx::cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)kPairSmem),
+                            "cudaFuncSetAttribute(gemm_pair)");
+    if (s) return s;
+    attr_set[dev & 63] = true;
+  }
+  const int64_t items = pair_items(a.M, a.N);
+  const int pairs = (int)std::min<int64_t>(items, device_sms() / 2);
+  int s = hx::cuda_status(launch_ex(kern, dim3((unsigned)(2 * pairs)), dim3(kGemmThreads),
+                                    kPairSmem, stream, 2, ma, mb, a),
+                          "gemm_pair_kernel launch");
+  if (s) return s;
+  HX_LAUNCH_CHECK("gemm_pair_kernel");
+  return HX_OK;
+}
+
+template <typename T, int EPI>
 int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int64_t K,
               int64_t lda, int64_t ldb, int64_t ldc, const void* R, int64_t ldr, void* ws,
               size_t ws_bytes, int dtype, cudaStream_t stream, const QkvArgs* qkv = nullptr) {
@@ -968,6 +1238,14 @@ int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int6
   }
   CUtensorMap ma, mb;
   int s;
+  if (p.pair) {
+    // Each CTA of a pair loads 128 rows of A and 128 rows (output columns) of B per k-block.
+    s = make_map(&ma, A, M, K, lda, BM, dtype);
+    if (s) return s;
+    s = make_map(&mb, B, N, K, ldb, BM, dtype);
+    if (s) return s;
+    return launch_pair<T, EPI>(ma, mb, a, stream);
+  }
   if (p.swap) {
     // MMA A = weights (128-row boxes), MMA B = activations (bn-row box).
     s = make_map(&ma, B, N, K, ldb, BM, dtype);
@@ -1044,6 +1322,13 @@ int gemm_f32(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int64
 }  // namespace
 
 extern "C" {
+
+int hx_gemm_kernel_kind(int64_t m, int64_t n, int64_t k, int dtype) {
+  if (m <= 0 || n <= 0 || k <= 0) return -1;
+  if (dtype == HX_F32) return 0;
+  const Plan p = plan_gemm(m, n, k);
+  return p.swap ? 3 : (p.pair ? 2 : 1);
+}
 
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;

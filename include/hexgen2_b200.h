@@ -118,6 +118,11 @@ int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t
  * problems, m <= 64, reduce their K splits inside a thread-block cluster and never need one).
  * Calls that run concurrently need separate workspaces. */
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
+/* Which kernel hx_gemm plans for a shape (host-only query, no GPU work): 0 CUDA-core f32,
+ * 1 single-SM tcgen05 tiles (128 x 64..256, K split when the tiles are too few), 2 CTA-pair
+ * tcgen05 tiles (256 x 256 over two SMs, cta_group::2), 3 decode-shaped (m <= 64: operands
+ * swapped, K split inside a cluster). Diagnostic; no reference counterpart. */
+int hx_gemm_kernel_kind(int64_t m, int64_t n, int64_t k, int dtype);
 
 /* Wqkv projection fused with rotary and the KV-cache write: computes qkv = x * Wqkv^T
  * ([m, (n_heads + 2*n_heads_kv) * head_dim], f32 accumulation, rounded to dtype like the

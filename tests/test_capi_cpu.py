@@ -42,6 +42,14 @@ def test_workspace_queries_need_no_gpu():
     # Decode-shaped bf16 GEMMs reduce inside a cluster: no workspace.
     assert lib.hx_gemm_workspace(32, 4096, 4096, 0, _lib.HX_BF16) == 0
     assert lib.hx_gemm_workspace(300, 512, 2048, 0, _lib.HX_BF16) > 0
+    # Prefill shapes with enough 256 x 256 items run on CTA pairs (no workspace); small ones
+    # on single-SM tiles; m <= 64 is decode-shaped.
+    assert lib.hx_gemm_kernel_kind(900, 4096, 4096, _lib.HX_BF16) == 2
+    assert lib.hx_gemm_workspace(900, 4096, 4096, 0, _lib.HX_BF16) == 0
+    assert lib.hx_gemm_kernel_kind(300, 512, 2048, _lib.HX_BF16) == 1
+    assert lib.hx_gemm_kernel_kind(128, 22016, 4096, _lib.HX_BF16) == 1
+    assert lib.hx_gemm_kernel_kind(32, 4096, 4096, _lib.HX_BF16) == 3
+    assert lib.hx_gemm_kernel_kind(900, 4096, 4096, _lib.HX_F32) == 0
     # head_dim 32: one key split, no partials; head_dim 128: the balanced path's partials.
     assert lib.hx_decode_attention_workspace(1, 32, 32, 16) == 0
     assert lib.hx_decode_attention_workspace(1, 32, 128, 16) > 0

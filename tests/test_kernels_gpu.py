@@ -130,6 +130,36 @@ def test_gemm_epilogues(ops, M, N, K):
     torch.testing.assert_close(r.cpu().float(), gemm_ref(a, b, 1, res, dt).float(), rtol=2 ** -6, atol=2e-2)
 
 
+# Shapes that run on CTA pairs (256 x 256 tiles over two SMs): M tails that leave the odd CTA's
+# rows wholly out of range (300, 257), an N tail that does the same for its columns (16000),
+# long K, and the model's projection shapes at a 900-token prompt.
+PAIR_SHAPES = [(900, 4096, 4096), (1000, 12288, 1024), (300, 22016, 512), (257, 16000, 256),
+               (900, 4096, 11008), (640, 8192, 520)]
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+def test_gemm_cta_pairs(ops, M, N, K):
+    from hexgen2_b200 import _lib
+    assert _lib.lib().hx_gemm_kernel_kind(M, N, K, _lib.HX_BF16) == 2
+    dt = torch.bfloat16
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g).to(dt)
+    b = (torch.randn(N, K, generator=g) * 0.05).to(dt)
+    res = torch.randn(M, N, generator=g).to(dt)
+    out = ops.gemm(a.cuda(), b.cuda()).cpu()
+    torch.testing.assert_close(out.float(), gemm_ref(a, b, 0, None, dt).float(), rtol=2 * ulp_tol(dt), atol=1e-3)
+    out = ops.gemm(a.cuda(), b.cuda(), ops.HX_EPI_RESIDUAL, residual=res.cuda()).cpu()
+    # round(round(acc) + r): a summation-order flip of the inner rounding moves the result by
+    # one ulp of acc, which the residual add does not shrink, so bound by both ulps.
+    ref = gemm_ref(a, b, 1, res, dt).float()
+    acc = a.float() @ b.float().T
+    bound = acc.abs() * 2 ** -7 + ref.abs() * 2 ** -7 + 1e-3
+    assert ((out.float() - ref).abs() <= bound).all(), (out.float() - ref).abs().max()
+    out = ops.gemm(a.cuda(), b.cuda(), ops.HX_EPI_SWIGLU).cpu()
+    torch.testing.assert_close(out.float(), gemm_ref(a, b, 2, None, dt).float(), rtol=2 ** -5, atol=2e-3)
+    assert ops.device_error() == 0
+
+
 @pytest.mark.parametrize("epi", [0, 1, 2])
 def test_gemm_f32(ops, epi):
     g = torch.Generator().manual_seed(epi)
@@ -373,7 +403,8 @@ def test_errors_are_reported_not_crashes(ops):
 
 # ------------------------------------------------------------------------------ fused Wqkv
 @pytest.mark.parametrize("B,S,hq,hk,d", [(4, 1, 32, 32, 128), (32, 1, 32, 32, 128), (1, 300, 32, 4, 64),
-                                         (2, 77, 8, 2, 128), (64, 1, 16, 2, 128), (3, 1, 4, 2, 32)])
+                                         (2, 77, 8, 2, 128), (64, 1, 16, 2, 128), (3, 1, 4, 2, 32),
+                                         (1, 1000, 32, 8, 128), (2, 450, 32, 32, 128)])
 def test_gemm_qkv_rotary_matches_separate_path(ops, B, S, hq, hk, d):
     """Wqkv GEMM with rotary + cache write in its epilogue == GEMM, then hx_rotary_cache_write."""
     dt, h = torch.bfloat16, hq * d
