@@ -21,7 +21,33 @@ __global__ void argmax_kernel(const T* __restrict__ logits, int64_t cols, int64_
   const T* row = logits + (int64_t)blockIdx.x * ld;
   float bv = -INFINITY;
   int64_t bi = cols;  // sentinel larger than any index
-  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) better(bv, bi, DT<T>::to_f(row[i]), i);
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte load
+  if (sizeof(T) < 4 && ((uintptr_t)row % 16) == 0) {
+    // 16-byte loads, four in flight per thread before any compare; the order of the compares
+    // does not matter (better() prefers the larger value, then the smaller index).
+    const int64_t nvec = cols / V;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    for (int64_t base = threadIdx.x; base < nvec; base += 4 * (int64_t)blockDim.x) {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t vi = base + (int64_t)u * blockDim.x;
+        raw[u] = vi < nvec ? rv[vi] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t vi = base + (int64_t)u * blockDim.x;
+        if (vi >= nvec) break;
+        const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+        for (int j = 0; j < V; ++j) better(bv, bi, DT<T>::to_f(e[j]), vi * V + j);
+      }
+    }
+    for (int64_t i = nvec * V + threadIdx.x; i < cols; i += blockDim.x)
+      better(bv, bi, DT<T>::to_f(row[i]), i);
+  } else {
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) better(bv, bi, DT<T>::to_f(row[i]), i);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     float ov = __shfl_xor_sync(0xffffffffu, bv, o);

@@ -1084,9 +1084,12 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
   Plan p;
   p.k_blocks = ceil_div(K, BK);
   p.swap = M <= 64;
-  // CTA pairs when there are rows for both halves and enough 256 x 256 items to occupy ~80%
-  // of the pairs in one wave; otherwise single-SM tiles with a K split.
-  p.pair = !p.swap && M > BM && N >= 256 && pair_items(M, N) * 5 >= (int64_t)(sms / 2) * 4;
+  // CTA pairs when there are rows for both halves and at least ~3/7 of the pairs get an item:
+  // a pair moves half the shared-memory bytes per FLOP of a single-SM tile, so even a partly
+  // filled wave of pairs beats two waves of shared-memory-bound single-SM tiles (measured at
+  // 900 rows: 64 items on 74 pairs 34 us vs 2 x 148 single-SM 128 x 128 tiles). Below that
+  // (M <= 256, or narrow N), single-SM tiles with a K split.
+  p.pair = !p.swap && M > BM && N >= 256 && pair_items(M, N) * 7 >= (int64_t)(sms / 2) * 3;
   int splits = 1;
   if (p.pair) {
     p.bn = 256;

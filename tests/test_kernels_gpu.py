@@ -132,9 +132,10 @@ def test_gemm_epilogues(ops, M, N, K):
 
 # Shapes that run on CTA pairs (256 x 256 tiles over two SMs): M tails that leave the odd CTA's
 # rows wholly out of range (300, 257), an N tail that does the same for its columns (16000),
-# long K, and the model's projection shapes at a 900-token prompt.
+# long K, the model's projection shapes at a 900-token prompt, and partly filled waves (48 and
+# 32 items on 74 pairs).
 PAIR_SHAPES = [(900, 4096, 4096), (1000, 12288, 1024), (300, 22016, 512), (257, 16000, 256),
-               (900, 4096, 11008), (640, 8192, 520)]
+               (900, 4096, 11008), (640, 8192, 520), (700, 4096, 2048), (285, 4096, 1024)]
 
 
 @pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
@@ -332,16 +333,23 @@ def test_reshard_kv_matches_reference_head_concat(ops, src_tp, dst_tp):
 
 
 # ------------------------------------------------------------------------------ argmax
-@pytest.mark.parametrize("dtype", ["bf16", "f32"])
-def test_argmax_ties_first_index(ops, dtype):
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("cols", [32000, 32003, 7])
+def test_argmax_ties_first_index(ops, dtype, cols):
     dt = DT[dtype]
-    x = torch.randn(6, 32000).to(dt)
-    x[1, 100] = x[1, 5000] = 50.0
+    x = torch.randn(7, cols).to(dt)
+    x[1, 1] = x[1, cols - 2] = 50.0
     x[2, :] = 1.0
-    x[3, 31999] = 99.0
+    x[3, cols - 1] = 99.0
+    x[4, 3] = float("nan")  # NaN is the maximum, like torch.argmax
     out = ops.argmax(x.cuda()).cpu()
     assert out.tolist() == x.argmax(-1).tolist()
-    assert out[2].item() == 0 and out[1].item() == 100
+    assert out[2].item() == 0 and out[1].item() == 1 and out[4].item() == 3
+    # Row-strided view whose rows start off a 16-byte boundary (scalar path).
+    wide = torch.randn(7, cols + 1).to(dt)
+    wide[:, 1:] = x
+    got = ops.argmax(wide.cuda()[:, 1:]).cpu()
+    assert got.tolist() == x.argmax(-1).tolist()
 
 
 # ------------------------------------------------------------------------------ KV pack
