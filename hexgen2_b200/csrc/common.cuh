@@ -171,7 +171,7 @@ HX_DEVICE void named_bar_sync(int id, int count) {
 
 // ---------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) — tiled 2D/3D loads into this CTA's shared memory.
-// No cluster multicast anywhere in this library.
+// Every tensor load here fills only the issuing CTA's own shared memory (one CTA per copy).
 // ---------------------------------------------------------------------------------------
 HX_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                            int32_t y) {
