@@ -422,7 +422,9 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
         }
       }
     }
-    named_barrier_consumers();
+    // No barrier here: the next piece writes q_s (read only in the tile loops, which every
+    // thread left before the barrier above) and then meets at its own start barrier before
+    // anything rewrites mo / ml.
     pc = pn;
     have = have_next;
   }
