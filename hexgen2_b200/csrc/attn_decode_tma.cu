@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kThreadsTma, 1)
       // Loads older than the last kStages were released by the consumers before their stage
       // was reused; let the newest ones land (bounded) before this warp leaves.
       for (uint32_t i = issued > (uint32_t)L::kStages ? issued - L::kStages : 0; i < issued; ++i)
-        mbar_wait(&full[i % L::kStages], (i / L::kStages) & 1);
+        mbar_wait_drain(&full[i % L::kStages], (i / L::kStages) & 1);
     }
     return;  // the producer warp takes no part in the consumer barriers below
   }
@@ -662,23 +662,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     if (lane == 0 && u0 < u1) {
       TileWalker tw(pre, hkv, a.batch, u0, u1);
-      int j = 0;
+      int j = 0, nq = 0;  // K/V tiles and query rows issued
+      bool aborted = false;
       while (tw.next()) {
         if (tw.first()) {
           const int qb = tw.piece & 1;
-          if (!mbar_wait(&q_empty[qb], ((tw.piece >> 1) & 1) ^ 1)) break;
+          if (!mbar_wait(&q_empty[qb], ((tw.piece >> 1) & 1) ^ 1)) { aborted = true; break; }
           mbar_arrive_expect_tx(&q_full[qb], L::kQBytes);
           const int row = tw.p.b * a.n_heads + tw.p.hk * G;
 #pragma unroll
           for (int c = 0; c < L::kChunks; ++c)
             tma_load_2d(sm + L::kQ + qb * L::kQBytes + c * kNq * 128, &tmQ, &q_full[qb], c * 64, row);
+          ++nq;
         }
         const int st = j % L::kStages;
-        if (!mbar_wait(&kv_empty[st], ((j / L::kStages) & 1) ^ 1)) break;
+        if (!mbar_wait(&kv_empty[st], ((j / L::kStages) & 1) ^ 1)) { aborted = true; break; }
         load_kv_tile<L::kChunks>(sm + st * L::kStageBytes, &kv_full[st], &tmKV, &tmKV32, tw.p.hk,
                                  hkv, tw.t * kTileKeys, tw.p.b,
                                  live_len(a, tw.p.b) - tw.t * kTileKeys);
         ++j;
+      }
+      if (aborted) {
+        // The consumers may have given up as well: let the newest loads (each the latest use of
+        // its buffer) land before the CTA's shared memory is released.
+        for (int i = j > L::kStages ? j - L::kStages : 0; i < j; ++i)
+          mbar_wait_drain(&kv_full[i % L::kStages], (i / L::kStages) & 1);
+        for (int i = nq > 2 ? nq - 2 : 0; i < nq; ++i) mbar_wait_drain(&q_full[i & 1], (i >> 1) & 1);
       }
     }
   } else if (warp == 1) {

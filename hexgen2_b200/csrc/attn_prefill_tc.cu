@@ -388,11 +388,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   // After an aborted wait, let issued-but-unconsumed TMA loads land (bounded) before exit.
   if (threadIdx.x == 0) {
-    if (!counters[2]) mbar_wait(q_full, 0);
+    if (!counters[2]) mbar_wait_drain(q_full, 0);
     for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait(&k_full[i & 1], (i >> 1) & 1)) break;
+      if (!mbar_wait_drain(&k_full[i & 1], (i >> 1) & 1)) break;
     for (uint32_t i = counters[4]; i < counters[3]; ++i)
-      if (!mbar_wait(&v_full[i & 1], (i >> 1) & 1)) break;
+      if (!mbar_wait_drain(&v_full[i & 1], (i >> 1) & 1)) break;
   }
   __syncthreads();
   tc_fence_after();

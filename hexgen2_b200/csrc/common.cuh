@@ -144,6 +144,20 @@ HX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Wait used when a CTA is about to exit after an aborted wait: lets TMA loads that were issued
+// but never consumed land before the CTA's shared memory is released. Unlike mbar_wait it does
+// not give up when another CTA has recorded an error (that is exactly when it runs), only after
+// HX_DRAIN_LIMIT_NS.
+static constexpr unsigned long long HX_DRAIN_LIMIT_NS = 200000000ull;  // 200 ms
+HX_DEVICE bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < HX_DRAIN_LIMIT_NS)
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
 // Bounded wait by a whole warp with a warp-uniform result, for code that follows the wait with
 // warp-collective instructions (tcgen05.ld, shuffles): every lane leaves together.
 HX_DEVICE bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {

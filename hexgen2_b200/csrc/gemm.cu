@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // (bounded) before the CTA's shared memory goes away.
   if (threadIdx.x == 0) {
     for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1)) break;
+      if (!mbar_wait_drain(&full[i % C::kStages], (i / C::kStages) & 1)) break;
   }
   __syncthreads();
   tc_fence_after();
@@ -720,7 +720,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // (bounded) before the CTA's shared memory goes away.
   if (threadIdx.x == 0) {
     for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait(&full[i % stages], (i / stages) & 1)) break;
+      if (!mbar_wait_drain(&full[i % stages], (i / stages) & 1)) break;
   }
   __syncthreads();
   tc_fence_after();
@@ -1051,7 +1051,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // memory goes away; they all complete on the even CTA's barriers.
   if (threadIdx.x == 0 && even) {
     for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait(&full[i % kPairStages], (i / kPairStages) & 1)) break;
+      if (!mbar_wait_drain(&full[i % kPairStages], (i / kPairStages) & 1)) break;
   }
   __syncthreads();
   cluster_sync_all();  // no CTA leaves while its peer may still signal or read it
