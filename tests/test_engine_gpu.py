@@ -171,7 +171,9 @@ def test_disaggregated_equals_colocated(hx, fixture_dir):
     first, cache, _ = a.prefill(prompt, 12)
     moved = {k: v.clone() for k, v in cache.items()}
     del cache
-    t1 = b.decode(first, moved, len(prompt), 12)
+    seen = []  # on_token sees every generated token in order, the first one included
+    t1 = b.decode(first, moved, len(prompt), 12, on_token=seen.append)
+    assert seen == t1
     f2, c2, _ = a.prefill(prompt, 12)
     t2 = a.decode(f2, c2, len(prompt), 12)
     assert t1 == t2
