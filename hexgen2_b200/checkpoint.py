@@ -58,18 +58,33 @@ def config_from_dict(d: dict):
     return llama_config_to_gpt2_config(LlamaConfig(**d))
 
 
+def _pad_rows(w: torch.Tensor, multiple: int) -> torch.Tensor:
+    rows = math.ceil(w.shape[0] / multiple) * multiple
+    if rows == w.shape[0]:
+        return w
+    return torch.cat([w, w.new_zeros(rows - w.shape[0], *w.shape[1:])], dim=0)
+
+
 def remap_state_dict_hf_llama(state_dict: dict, config) -> dict:
     """HF Llama names/layout -> native names/layout (remap_state_dict.py:14-115):
     fc1 = cat[up, gate]; Wqkv = cat[inv_permute(Wq), inv_permute(Wk), Wv] where inv_permute
-    reorders each head's rows from (two, d/2) to (d/2, two) so rotary pairs are adjacent."""
+    reorders each head's rows from (two, d/2) to (d/2, two) so rotary pairs are adjacent.
+    The embedding and the LM head are zero-padded to a multiple of
+    config.pad_vocab_size_multiple rows (:28-51); with config.tie_word_embeddings the LM head is
+    the embedding, otherwise lm_head.weight must be present (a missing one raises KeyError,
+    as in the reference)."""
     n_embd = getattr(config, "n_embd", None) or config.hidden_size
     n_head = getattr(config, "n_head", None) or config.num_attention_heads
     half = n_embd // n_head // 2
+    multiple = getattr(config, "pad_vocab_size_multiple", 1) or 1
     sd = OrderedDict(state_dict)
     out = OrderedDict()
-    out["transformer.embeddings.word_embeddings.weight"] = sd.pop("model.embed_tokens.weight")
-    out["lm_head.weight"] = sd.pop("lm_head.weight") if "lm_head.weight" in sd else \
-        out["transformer.embeddings.word_embeddings.weight"]
+    emb = _pad_rows(sd.pop("model.embed_tokens.weight"), multiple)
+    out["transformer.embeddings.word_embeddings.weight"] = emb
+    if getattr(config, "tie_word_embeddings", False):
+        out["lm_head.weight"] = emb
+    else:
+        out["lm_head.weight"] = _pad_rows(sd.pop("lm_head.weight"), multiple)
     out["transformer.ln_f.weight"] = sd.pop("model.norm.weight")
 
     def inv_permute(w):

@@ -107,7 +107,8 @@ class Engine:
         L = len(input_ids)
         state = CacheState(L + max_new_tokens)
         logits = self.model(ids, inference_params=state, last_token_only=True).logits
-        # Send only initialized prompt positions, never the unused cache capacity.
+        # The returned cache holds the prompt's L written rows of every layer; the
+        # max_new_tokens rows reserved for decoding stay behind.
         cache = self.pack_live(state.key_value_memory_dict, [L])[0]
         return ops.argmax(logits), cache, logits
 
@@ -234,9 +235,9 @@ class Engine:
         cur.copy_(tokens[0].view(B, 1))
 
         def step():
-            logits = self.model(cur, inference_params=state, last_token_only=True).logits
+            nxt = self.model.next_tokens(cur, inference_params=state)
             lengths.add_(1)
-            ops.argmax(logits, out=cur.view(B))
+            cur.view(B).copy_(nxt)
 
         captured = []  # per-kernel event pairs recorded as graph nodes (profiling only)
         for s in range(steps):

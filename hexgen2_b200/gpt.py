@@ -297,7 +297,12 @@ class GPTLMHeadModel(nn.Module):
 
     # ------------------------------------------------------------------ forward
     @torch.inference_mode()
-    def forward(self, input_ids, position_ids=None, inference_params=None, last_token_only=False):
+    def forward(self, input_ids, position_ids=None, inference_params=None, last_token_only=False,
+                gather_logits=True):
+        """gpt.py:463-483. With tensor parallelism the LM head is vocab-parallel; its logits are
+        all-gathered into [.., vocab] as in the reference (gpt.py:479-481) unless gather_logits
+        is False, in which case this rank's vocabulary slice is returned (next_tokens() uses
+        that to pick the greedy token without gathering the logits)."""
         if input_ids.dim() != 2:
             raise ValueError("input_ids must be [batch, seqlen]")
         B, S = input_ids.shape
@@ -387,10 +392,42 @@ class GPTLMHeadModel(nn.Module):
         else:
             hfin = ops.rmsnorm(residual, self.transformer.ln_f.weight, self.eps)
         logits = ops.gemm(hfin, self.lm_head.weight)
-        if self.tp > 1:
+        if self.tp > 1 and gather_logits:
             parts = [torch.empty_like(logits) for _ in range(self.tp)]
             dist.all_gather(parts, logits, group=self.process_group)
             logits = torch.cat(parts, dim=-1)
         if not last_token_only:
             logits = logits.view(B, S, -1)
         return CausalLMOutput(logits=logits)
+
+    @torch.inference_mode()
+    def next_tokens(self, input_ids, inference_params=None, out=None):
+        """Greedy next token of every sequence: argmax of forward(..., last_token_only=True)
+        with torch.argmax's tie rule (lowest vocabulary index). Returns int64 [batch].
+
+        With tensor parallelism each rank takes the argmax of its own vocabulary slice and the
+        ranks agree on the winner with ONE all-reduce(MAX) of one int64 key per sequence: the
+        high 32 bits order the logit value (its f32 bit pattern mapped to a signed integer of the
+        same order), the low 32 bits are (2^32 - 1 - global index), so equal values resolve to
+        the lowest index, as on the gathered logits. This replaces the all-gather of
+        [batch, vocab / TP] logits (gpt.py:479-481) on the decode path."""
+        logits = self.forward(input_ids, inference_params=inference_params, last_token_only=True,
+                              gather_logits=False).logits
+        if self.tp == 1:
+            return ops.argmax(logits, out=out)
+        return self._tp_argmax(logits, out)
+
+    def _tp_argmax(self, local_logits, out=None):
+        rows, vloc = local_logits.shape
+        idx = ops.argmax(local_logits)
+        val = local_logits.gather(1, idx.view(rows, 1)).view(rows).float()
+        bits = val.view(torch.int32)
+        ordered = torch.where(bits < 0, bits ^ 0x7FFFFFFF, bits).to(torch.int64)
+        gidx = idx + _pg_rank(self.process_group) * vloc
+        key = ordered * 4294967296 + (4294967295 - gidx)
+        dist.all_reduce(key, op=dist.ReduceOp.MAX, group=self.process_group)
+        win = 4294967295 - (key & 4294967295)
+        if out is None:
+            return win
+        out.copy_(win)
+        return out

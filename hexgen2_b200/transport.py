@@ -346,10 +346,13 @@ def unpack_kv_heads(src, src_offsets: list[int], caches: dict, rows: list[int],
 def reshard_kv(src_caches: list[dict], dst_caches: list[dict], rows: list[int],
                lengths: list[int], n_kv_heads: int):
     """Moves the live rows of requests `rows` from caches sharded over len(src_caches) TP ranks
-    into caches sharded over len(dst_caches) ranks, all on this process's devices: for every
-    move of reshard_plan, one pack into a staging buffer on the source's device and one unpack
-    into the destination (peer reads when the two differ). Across processes the same moves run
-    with the staging buffer exposed through KVHandoff."""
+    into caches sharded over len(dst_caches) ranks, all held by this process (one device or
+    several): for every move of reshard_plan, one pack into a staging buffer on the source's
+    device (launched with that device current, on its current stream) and one unpack into the
+    destination with the destination's device current. When the two devices differ the staging
+    buffer is first copied to the destination's device (torch orders that copy after the pack
+    and before the unpack), so no kernel dereferences another GPU's memory. Across processes the
+    same moves run with the staging buffer exposed through KVHandoff."""
     src_tp, dst_tp = len(src_caches), len(dst_caches)
     hs, hd = n_kv_heads // src_tp, n_kv_heads // dst_tp
     for s, t, lo, hi in reshard_plan(n_kv_heads, src_tp, dst_tp):
@@ -359,8 +362,11 @@ def reshard_kv(src_caches: list[dict], dst_caches: list[dict], rows: list[int],
         for b in sizes:
             offs.append(o)
             o += (b + 15) // 16 * 16
-        staging = torch.empty(max(o, 16), dtype=torch.uint8, device=src_caches[s][0].device)
-        pack_kv_heads(src_caches[s], rows, lengths, lo - s * hs, hi - s * hs, staging, offs)
-        if staging.device != dst_caches[t][0].device:
-            staging = staging.to(dst_caches[t][0].device)
-        unpack_kv_heads(staging, offs, dst_caches[t], rows, lengths, lo - t * hd, hi - t * hd)
+        src_dev, dst_dev = src_caches[s][0].device, dst_caches[t][0].device
+        with torch.cuda.device(src_dev):
+            staging = torch.empty(max(o, 16), dtype=torch.uint8, device=src_dev)
+            pack_kv_heads(src_caches[s], rows, lengths, lo - s * hs, hi - s * hs, staging, offs)
+        with torch.cuda.device(dst_dev):
+            if staging.device != dst_dev:
+                staging = staging.to(dst_dev)
+            unpack_kv_heads(staging, offs, dst_caches[t], rows, lengths, lo - t * hd, hi - t * hd)

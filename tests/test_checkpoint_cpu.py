@@ -99,3 +99,84 @@ def _tp_worker(rank, rendezvous):
 
 def test_tensor_parallel_sharding_on_two_gloo_ranks(tmp_path):
     mp.spawn(_tp_worker, args=(str(tmp_path / "rv"),), nprocs=2, join=True)
+
+
+def _hf_state(cfg: dict, seed: int, with_lm_head: bool = True) -> dict:
+    """A small HF-named Llama state dict (seeded N(0, 0.02))."""
+    g = torch.Generator().manual_seed(seed)
+    h, I, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    d = h // cfg["num_attention_heads"]
+    hk = cfg["num_key_value_heads"]
+
+    def rnd(*s):
+        return torch.randn(*s, generator=g) * 0.02
+
+    sd = {"model.embed_tokens.weight": rnd(V, h), "model.norm.weight": torch.ones(h)}
+    if with_lm_head:
+        sd["lm_head.weight"] = rnd(V, h)
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        sd.update({p + "input_layernorm.weight": torch.ones(h),
+                   p + "post_attention_layernorm.weight": torch.ones(h),
+                   p + "self_attn.q_proj.weight": rnd(h, h),
+                   p + "self_attn.k_proj.weight": rnd(hk * d, h),
+                   p + "self_attn.v_proj.weight": rnd(hk * d, h),
+                   p + "self_attn.o_proj.weight": rnd(h, h),
+                   p + "mlp.gate_proj.weight": rnd(I, h), p + "mlp.up_proj.weight": rnd(I, h),
+                   p + "mlp.down_proj.weight": rnd(h, I)})
+    return sd
+
+
+ODD_VOCAB = dict(SMALL, vocab_size=61)
+
+
+@pytest.mark.parametrize("tied", [False, True])
+def test_remap_pads_vocab_and_ties_like_reference(tied):
+    """remap_state_dict.py:28-51: embedding and LM head zero-padded to pad_vocab_size_multiple
+    rows; tie_word_embeddings makes the LM head the (padded) embedding."""
+    cfg = config_from_dict(ODD_VOCAB)
+    cfg.pad_vocab_size_multiple = 8
+    cfg.tie_word_embeddings = tied
+    sd = _hf_state(ODD_VOCAB, seed=3, with_lm_head=not tied)
+    out = remap_state_dict_hf_llama(dict(sd), cfg)
+    emb, head = out["transformer.embeddings.word_embeddings.weight"], out["lm_head.weight"]
+    assert emb.shape[0] == 64 and head.shape[0] == 64
+    assert torch.equal(emb[:61], sd["model.embed_tokens.weight"]) and not emb[61:].any()
+    if tied:
+        assert head is emb
+    else:
+        assert torch.equal(head[:61], sd["lm_head.weight"]) and not head[61:].any()
+    # The padded state dict loads strictly into the model (which pads its vocab the same way).
+    model = GPTLMHeadModel(cfg, device="cpu", dtype=torch.float32)
+    model.load_state_dict(out, strict=True)
+
+
+def test_remap_untied_without_lm_head_raises():
+    """With tie_word_embeddings False a checkpoint without lm_head.weight is an error, as in the
+    reference (it pops the key unconditionally)."""
+    cfg = config_from_dict(SMALL)
+    with pytest.raises(KeyError):
+        remap_state_dict_hf_llama(_hf_state(SMALL, seed=4, with_lm_head=False), cfg)
+
+
+REF_REMAP = Path("/root/reference/hexgen/llama/load_model_parameters_utils/remap_state_dict.py")
+
+
+@pytest.mark.skipif(not REF_REMAP.exists(), reason="reference sources not mounted")
+@pytest.mark.parametrize("tied,multiple", [(False, 1), (False, 8), (True, 8)])
+def test_remap_equals_reference_remap(tied, multiple):
+    """The reference's own remap (imported from its source file) and this one produce the same
+    tensors for padded and tied configurations."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_ref_remap", REF_REMAP)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    cfg = config_from_dict(ODD_VOCAB)
+    cfg.pad_vocab_size_multiple = multiple
+    cfg.tie_word_embeddings = tied
+    sd = _hf_state(ODD_VOCAB, seed=5, with_lm_head=not tied)
+    ours = remap_state_dict_hf_llama(dict(sd), cfg)
+    theirs = ref.remap_state_dict_hf_llama(dict(sd), cfg)
+    assert set(ours) == set(theirs)
+    for k in theirs:
+        assert torch.equal(ours[k], theirs[k]), k

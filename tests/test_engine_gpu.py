@@ -31,25 +31,19 @@ def hx():
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
-def test_engine_matches_reference_golden(hx, golden, fixture_dir, dtype):
+def test_engine_prefill_matches_reference_golden(hx, golden, fixture_dir, dtype):
+    """Prefill logits against the reference's golden bits and the returned cache shapes.
+    Decode logits and greedy tokens are checked step by step in test_parity_gpu.py."""
     eng = hx.Engine(fixture_dir, device="cuda", dtype=dtype)
     tol = 1e-4 if dtype == "float32" else 2e-2
-    mismatched = []
     for row in golden["engine"][dtype]:
         first, cache, logits = eng.prefill(row["prompt"], row["max_new"])
         expected = from_bits(row["prefill_logits"], getattr(torch, dtype)).float()
         torch.testing.assert_close(logits[0].float().cpu(), expected, rtol=0, atol=tol)
         for k, meta in row["kv"].items():
             assert list(cache[int(k)].shape) == meta["shape"]
-        tokens = eng.decode(first, cache, len(row["prompt"]), row["max_new"])
-        if tokens != row["tokens"]:
-            mismatched.append((row["name"], tokens, row["tokens"]))
-    if dtype == "float32":
-        assert not mismatched, mismatched
-    else:
-        # Half precision: divergence must be explained by a near-tie (checked with the oracle in
-        # test_bf16_token_divergence_is_a_near_tie); at least 8 of 10 cases must match exactly.
-        assert len(mismatched) <= 2, mismatched
+        if dtype == "float32":
+            assert int(first) == row["first_token"]
 
 
 def test_prefill_cache_is_bit_exact_in_f32(hx, golden, fixture_dir):

@@ -118,3 +118,60 @@ def test_reshard_plan_rejects_indivisible_sizes():
         reshard_plan(8, 3, 2)
     with pytest.raises(ValueError):
         reshard_plan(8, 2, 0)
+
+
+REF_TRANSPORT = Path("/root/reference/hexgen2/transport.py")
+
+
+def _load_reference_transport():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_ref_transport", REF_TRANSPORT)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _interop_worker(rank, rendezvous):
+    """Rank 0 runs this package's transport, rank 1 the reference's own module (imported
+    unchanged from its source file); packets go both ways for every KV dtype."""
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=2, init_method=Path(rendezvous).as_uri(),
+                            timeout=timedelta(seconds=30))
+    try:
+        ref = _load_reference_transport()
+        for dtype in (torch.float16, torch.bfloat16, torch.float32):
+            # A prefill result as this package returns it: per-layer contiguous views of ONE
+            # packed buffer ([1, L, 2, hkv, d] each), plus the first token.
+            L, layers, hk, d = 5, 3, 2, 8
+            buf = torch.arange(layers * L * 2 * hk * d, dtype=torch.float32).to(dtype)
+            view = buf.view(layers, 1, L, 2, hk, d)
+            cache = {i: view[i] for i in range(layers)}
+            token = torch.tensor([123], dtype=torch.long)
+            if rank == 0:
+                n = send_data(token, cache, dst=1)                       # ours -> reference
+                assert n == 8 + layers * L * 2 * hk * d * buf.element_size()
+                got_tok, got = recv_data(src=1, num_layers=layers)      # reference -> ours
+            else:
+                got_tok, got = ref.recv_data(src=0, num_layers=layers)
+                ref.send_data(got_tok, got, dst=0)
+            assert torch.equal(got_tok, token)
+            assert list(got) == list(range(layers))
+            for i in range(layers):
+                assert got[i].dtype == dtype and torch.equal(got[i], cache[i]), (dtype, i)
+        # Metadata and empty tensors, reference sender -> this receiver.
+        if rank == 1:
+            ref.send_packet({"e": torch.zeros(0, 3), "x": torch.ones(2, dtype=torch.int32)},
+                            {"request": "r-1", "layers": []}, dst=0)
+        else:
+            t, meta = recv_packet(src=1)
+            assert meta == {"request": "r-1", "layers": []}
+            assert t["e"].shape == (0, 3) and t["x"].dtype == torch.int32
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not REF_TRANSPORT.exists(), reason="reference sources not mounted")
+def test_interop_with_reference_transport(tmp_path):
+    """This package's send_packet/send_data feed the reference's recv_packet/recv_data and the
+    reverse (hexgen2/transport.py:44-100), on a real 2-process Gloo group."""
+    mp.spawn(_interop_worker, args=(str(tmp_path / "rendezvous"),), nprocs=2, join=True)
