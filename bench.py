@@ -39,6 +39,9 @@ LLAMA2_7B = dict(vocab_size=32000, hidden_size=4096, intermediate_size=11008,
                  num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=32,
                  rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=4096 + 512)
 METRIC = "decode tokens/s + p50 TTFT (Llama-2-7B arch, bf16)"
+VALUE_DEFINITION = ("generated tokens / device time of the timed steps, prefill included: the "
+                    "serving system's output-token throughput (decode_phase_tokens_per_s excludes "
+                    "prefill time)")
 
 
 def prompt_lengths(batch: int, seed: int) -> list[int]:
@@ -119,48 +122,146 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------
 # Native arm, N = 1 (colocated)
 # ------------------------------------------------------------------------------------------
-def kernel_work(cfg: dict, lens: list[int], out_len: int, steps: int) -> dict:
-    """Algorithmic bytes / flops per kernel class over `steps` bench steps (for the roofline).
-    decode_attention: live K and V of every sequence, every layer, every decode step (+ q, out);
-    gemm_decode: every weight matrix once per decode step, plus the LM head of each prefill;
-    gemm_prefill: 2 * tokens * (layer weights) per prompt; prefill_attention: 4 * hq * d * L^2 / 2
-    per layer (causal)."""
-    h, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"]
+# DRAM bytes per algorithmic byte of each decode-step kernel class, from the ncu capture
+# summarised in profiles/decode_step_dram_llama7b_b32.md (dram__bytes_read.sum +
+# dram__bytes_write.sum over one decode step's launches of the class / the algorithmic bytes of
+# those launches). bench.py cannot run ncu; it scales its own algorithmic bytes by these.
+DRAM_PER_ALGORITHMIC = {"gemm_decode": 1.006, "decode_attention": 1.004, "rmsnorm": 1.0}
+DRAM_SOURCE = "profiles/decode_step_dram_llama7b_b32.md (ncu dram__bytes_read/write, scaled)"
+
+
+def layer_params(cfg: dict) -> int:
+    h, I = cfg["hidden_size"], cfg["intermediate_size"]
     hq, hk = cfg["num_attention_heads"], cfg["num_key_value_heads"]
     d = cfg.get("head_dim") or h // hq
-    B = len(lens)
-    layer_params = (hq + 2 * hk) * d * h + h * hq * d + 2 * I * h + h * I
-    dec_bytes = 0
-    for s in range(out_len - 1):
-        for Lb in lens:
-            dec_bytes += 2 * hk * d * (Lb + s + 1) * 2 + 2 * hq * d * 2
-    dec_bytes *= L
-    gemm_dec_bytes = (out_len - 1) * (L * layer_params + V * h) * 2 + B * V * h * 2
-    gemm_pre_flops = sum(2 * Lb * L * layer_params for Lb in lens)
-    attn_pre_flops = sum(4 * hq * d * Lb * Lb / 2 * L for Lb in lens)
-    return {"decode_attention": {"bytes": dec_bytes * steps},
-            "gemm_decode": {"bytes": gemm_dec_bytes * steps},
-            "gemm_prefill": {"flops": gemm_pre_flops * steps},
-            "prefill_attention": {"flops": attn_pre_flops * steps}}
+    return (hq + 2 * hk) * d * h + h * hq * d + 2 * I * h + h * I
 
 
-def rooflines(per_kernel: dict, work: dict, pk: dict) -> dict:
+def decode_step_bytes(cfg: dict, lens: list[int]) -> dict:
+    """Algorithmic HBM bytes of ONE decode step of a batch whose sequences hold `lens` keys,
+    per kernel class (bf16):
+      gemm_decode: every weight once (4 projections per layer + the LM head) + activations
+                   (inputs, outputs, residual reads);
+      decode_attention: the live K and V rows of every sequence in every layer + q and output;
+      rmsnorm: two norms per layer and the final one, read + write of [B, h] + the weight."""
+    h, I, V, nl = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"]
+    hq, hk = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    d = cfg.get("head_dim") or h // hq
+    B, e = len(lens), 2
+    qkv = (hq + 2 * hk) * d
+    acts = (B * h + B * hq * d + B * qkv) + (B * hq * d + 2 * B * h) + (B * h + B * I) + (B * I + 2 * B * h)
+    gemm = nl * (layer_params(cfg) * e + acts * e) + V * h * e + B * h * e + B * V * e
+    attn = nl * (sum(lens) * 2 * hk * d * e + 2 * B * hq * d * e)
+    norm = (2 * nl + 1) * (2 * B * h * e + h * e)
+    return {"gemm_decode": gemm, "decode_attention": attn, "rmsnorm": norm}
+
+
+def class_step_times(eng, cache, lens_mid: list[int], capacity: int, reps: int = 8) -> dict:
+    """Device time of one decode step's launches of each kernel class, each class alone: the
+    class's launches of one decode step (every layer, the model's own weights, the bench's own
+    cache at the given live lengths, batch B) are captured in one CUDA graph in step order, so
+    the programmatic-dependent-launch edges between consecutive launches are kept, and the
+    graph is replayed `reps` times between two CUDA events on the launching stream. No event
+    sits between kernels. Returns {class: (ms per decode step, launches)}."""
+    from hexgen2_b200 import ops
+    m = eng.model
+    dev, dt = eng.device, eng.dtype
+    B = len(lens_mid)
+    h, hq, hk, d = m.hidden, m.hq, m.hk, m.head_dim
+    layers = m.transformer.layers
+    I2 = layers[0].mlp.fc1.weight.shape[0]
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def rnd(*size):
+        return (torch.randn(*size, generator=g, device=dev, dtype=torch.float32) * 0.5).to(dt)
+
+    normed, res, ctx, act = rnd(B, h), rnd(B, h), rnd(B, hq * d), rnd(B, I2 // 2)
+    tmp = torch.empty(B, h, device=dev, dtype=dt)
+    q = torch.empty(B, hq, d, device=dev, dtype=dt)
+    attn_out = torch.empty(B, hq, d, device=dev, dtype=dt)
+    logits = torch.empty(B, m.lm_head.weight.shape[0], device=dev, dtype=dt)
+    pos = torch.tensor(lens_mid, dtype=torch.int32, device=dev) - 1
+    seqlens = pos + 1
+    cos, sin = m.rope_tables(capacity, dev, dt)
+
+    def gemms():
+        for i, layer in enumerate(layers):
+            ops.gemm_qkv_rotary(normed, layer.mixer.Wqkv.weight, 1, hq, hk, d, pos, cos, sin,
+                                cache[i], q_out=q)
+            ops.gemm(ctx, layer.mixer.out_proj.weight, ops.HX_EPI_RESIDUAL, residual=res, out=tmp)
+            ops.gemm(normed, layer.mlp.fc1.weight, ops.HX_EPI_SWIGLU, out=act)
+            ops.gemm(act, layer.mlp.fc2.weight, ops.HX_EPI_RESIDUAL, residual=res, out=tmp)
+        ops.gemm(normed, m.lm_head.weight, out=logits)
+
+    def attention():
+        for i in range(len(layers)):
+            ops.decode_attention(q, cache[i], seqlens, hk, capacity, m.scale, out=attn_out)
+
+    def norms():
+        for layer in layers:
+            ops.rmsnorm(res, layer.norm2.weight, m.eps, out=normed)
+            ops.rmsnorm(res, layer.norm1.weight, m.eps, out=normed)
+        ops.rmsnorm(res, m.transformer.ln_f.weight, m.eps, out=normed)
+
     out = {}
-    for name, w in work.items():
-        if name not in per_kernel:
-            continue
-        ms, n = per_kernel[name]
-        if "bytes" in w:
-            achieved = w["bytes"] / (ms / 1e3) / 1e9
-            peak, unit, bound = pk["hbm_gbs"], "GB/s", "hbm"
-        else:
-            achieved = w["flops"] / (ms / 1e3) / 1e12
-            peak, unit, bound = pk["bf16_tflops"], "TFLOP/s", "tensor"
-        out[name] = {"kernel": name, "bound": bound, "achieved": round(achieved, 1), "peak": peak,
-                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": None,
-                     "peak_source": pk["source"], "launches": n, "total_ms": round(ms, 2),
-                     "avg_launch_us": round(ms * 1e3 / n, 2),
-                     "timing": "CUDA events around every launch (graph nodes inside the decode graph), instrumented pass of the timed steps"}
+    for name, fn in (("gemm_decode", gemms), ("decode_attention", attention), ("rmsnorm", norms)):
+        fn()  # sizes scratch buffers outside the capture
+        torch.cuda.synchronize()
+        before = ops.LAUNCHES
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        launches = ops.LAUNCHES - before
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = (e0.elapsed_time(e1) / reps, launches)
+        del graph
+    return out
+
+
+def roofline_entries(times: dict, work: dict, pk: dict) -> dict:
+    out = {}
+    for name, (ms, launches) in times.items():
+        achieved = work[name] / (ms / 1e3) / 1e9
+        out[name] = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "traffic": int(work[name] * DRAM_PER_ALGORITHMIC[name]),
+                     "traffic_source": DRAM_SOURCE, "algorithmic_bytes": int(work[name]),
+                     "per": "one decode step of the class (%d launches)" % launches,
+                     "ms": round(ms, 4), "peak_source": pk["source"] + " (burst copy, of measured)",
+                     "timing": ("CUDA events around replays of a graph of one decode step's "
+                                "launches of this class alone (no event between kernels)")}
+    return out
+
+
+def prefill_latency(eng, lengths=(512, 1024), reps=5) -> dict:
+    """Isolated per-request prefill latency (batch 1, prompt ids already on the device, to the
+    greedy first token on the device), median of `reps` CUDA-event timings after a warm-up."""
+    from hexgen2_b200 import ops
+    from hexgen2_b200.gpt import CacheState
+    out = {}
+    g = torch.Generator().manual_seed(7)
+    for L in lengths:
+        ids = torch.randint(0, eng.config.vocab_size, (1, L), generator=g).to(eng.device)
+        cache = eng.model.allocate_inference_cache(1, L + 1)
+        times = []
+        for r in range(reps + 1):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            st = CacheState(L + 1, key_value_memory_dict=cache)
+            tok = ops.argmax(eng.model(ids, inference_params=st, last_token_only=True).logits)
+            e1.record()
+            torch.cuda.synchronize()
+            if r:
+                times.append(e0.elapsed_time(e1))
+        del tok
+        out[str(L)] = round(statistics.median(times), 3)
     return out
 
 
@@ -171,6 +272,8 @@ def run_native_single(args) -> dict:
 
     torch.cuda.set_device(0)
     cfg = dict(LLAMA2_7B)
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers  # profiling runs only (the line says so)
     eng = hx.Engine.from_config(cfg, dtype="bfloat16", seed=args.seed)
     model = eng.model
     B, out_len = args.batch, args.out_len
@@ -183,7 +286,7 @@ def run_native_single(args) -> dict:
     lengths = torch.empty(B, dtype=torch.int32, device="cuda")
     lens_dev = torch.tensor(lens, dtype=torch.int32, device="cuda")
 
-    def one_step(ttft_events, use_graph=True):
+    def one_step(ttft_events):
         for b in range(B):
             st = CacheState(capacity, max_batch_size=B, batch_size_offset=b,
                             key_value_memory_dict=cache)
@@ -195,7 +298,7 @@ def run_native_single(args) -> dict:
         dec0 = torch.cuda.Event(enable_timing=True)
         dec1 = torch.cuda.Event(enable_timing=True)
         dec0.record()
-        toks = eng.decode_batch(first, cache, lengths, out_len - 1, use_graph=use_graph)
+        toks = eng.decode_batch(first, cache, lengths, out_len - 1)
         dec1.record()
         return toks, dec0, dec1
 
@@ -225,61 +328,53 @@ def run_native_single(args) -> dict:
         if args.profile_region:
             torch.cuda.cudart().cudaProfilerStop()
     launches = ops.LAUNCHES
-    # Per-kernel durations: the same steps again, every kernel bracketed by CUDA events on the
-    # launching stream; inside the decode graph the events are graph nodes and are read after
-    # each replay (so no host submission gap is ever inside a measured interval).
-    prof = None
-    if args.profile_kernels:
-        ops.PROFILE = []
-        for _ in range(args.steps):
-            one_step(None)
-        torch.cuda.synchronize()
-        prof = ops.profile_durations(ops.PROFILE)
-        ops.PROFILE = None
     total_ms = t0.elapsed_time(t1)
     dec_ms = sum(a.elapsed_time(b) for a, b in decs)
     ttft_ms = [s.elapsed_time(e) for s, evs in zip(step_marks, ttfts) for e in evs]
-    dec_tokens = B * (out_len - 1) * args.steps
-    value = dec_tokens / (dec_ms / 1e3)
+    gen_tokens = B * out_len * args.steps
+    value = gen_tokens / (total_ms / 1e3)
+    decode_phase = B * (out_len - 1) * args.steps / (dec_ms / 1e3)
+    dec_step_ms = dec_ms / (args.steps * (out_len - 1))
 
-    # Per-kernel device time over the timed region.
-    per_kernel, per_shape = {}, {}
-    if prof:
-        for name, t in prof:
-            k = per_shape.setdefault(name, [0.0, 0])
-            k[0] += t
-            k[1] += 1
-            base = name.split("[")[0]
-            k = per_kernel.setdefault(base, [0.0, 0])
-            k[0] += t
-            k[1] += 1
-    work = kernel_work(cfg, lens, out_len, args.steps)
+    # Per-class device time of one decode step (each class alone, no events between kernels)
+    # at the batch's mean live lengths (mid-decode), against the same step's algorithmic bytes.
     pk = peaks()
-    roofs = rooflines(per_kernel, work, pk)
-    roofline = max(roofs.values(), key=lambda r: r["total_ms"]) if roofs else None
+    roofs, roofline = {}, None
+    if args.profile_kernels:
+        mid = [L + out_len // 2 for L in lens]
+        times = class_step_times(eng, cache, mid, capacity)
+        roofs = roofline_entries(times, decode_step_bytes(cfg, mid), pk)
+        roofline = dict(max(roofs.values(), key=lambda r: r["ms"]))
+        roofline["decode_step_ms_in_situ"] = round(dec_step_ms, 4)
+        roofline["classes_sum_ms"] = round(sum(r["ms"] for r in roofs.values()), 4)
 
     # End to end through the public API: pinned host prompts in, host token lists out.
     e2e = run_e2e(eng, prompts, out_len, args) if args.e2e_steps > 0 else None
+    latency = prefill_latency(eng) if args.profile_kernels else None
 
-    # Serial reference-algorithm baseline on the host cores (bounded sample).
-    cpu = cpu_baseline(args) if args.cpu_baseline else None
+    # Reference algorithm on the host cores (bounded sample of the same workload).
+    cpu = cpu_baseline(args, prompts, out_len) if args.cpu_baseline else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights, uniform token ids, lognormal prompt lengths)",
+        "value_definition": VALUE_DEFINITION,
+        "decode_phase_tokens_per_s": round(decode_phase, 2),
+        "decode_step_ms": round(dec_step_ms, 4),
         "ttft_p50_ms": round(statistics.median(ttft_ms), 2),
+        "ttft_definition": ("first token ready on the device - start of the step (the 32 prompts "
+                            "are prefilled one after another, batch 1 each)"),
+        "prefill_latency_ms": latency,
         "config": {"workload": "Llama-2-7B arch colocated on 1 GPU (BASELINE config 3, 1-GPU sweep)",
-                   "model": "llama-2-7b-arch", "batch": B, "prompt_lens_mean": round(sum(lens) / B, 1),
+                   "model": "llama-2-7b-arch", "layers": cfg["num_hidden_layers"], "batch": B,
+                   "prompt_lens_mean": round(sum(lens) / B, 1),
                    "prompt_lens_minmax": [min(lens), max(lens)], "output_len": out_len,
                    "parallelism": "colocated prefill+decode, TP1",
                    "l2": "inputs larger than L2 (13.5 GB weights + KV caches stream every step)"},
         "e2e": e2e, "gpu_launches": launches, "roofline": roofline, "rooflines": roofs,
         "clocks": clocks.summary(), "cpu_baseline": cpu,
         "decode_ms_per_step": [round(a.elapsed_time(b), 2) for a, b in decs],
-        "kernel_ms": {k: round(v[0], 2) for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])},
-        "gemm_decode_us": {k.split("[")[1][:-1]: round(v[0] * 1e3 / v[1], 2)
-                           for k, v in per_shape.items() if k.startswith("gemm_decode[")},
     }
     return line
 
@@ -307,57 +402,132 @@ def run_e2e(eng, prompts, out_len, args) -> dict:
 
 
 # ------------------------------------------------------------------------------------------
-# Reference algorithm on the CPU (the oracle port): bounded sample, extrapolated per layer.
+# Reference algorithm on the CPU (the oracle port): the bench's own batch, one layer timed.
 # ------------------------------------------------------------------------------------------
-def cpu_baseline(args, threads=None) -> dict:
-    from oracle.llama_ref import LlamaShape, OracleModel, random_native_state
+class CpuSample:
+    """The reference algorithm (oracle, torch bf16 on the host cores) on ONE of the 32
+    Llama-2-7B layers plus the embedding and LM head, on the bench's own workload: the same 32
+    prompts prefilled one after another at batch 1 (the reference Engine's prefill), then the
+    ragged batch of 32 decoded together (oracle.llama_ref.RaggedBatch). The full-model figure
+    is extrapolated: 32 x the per-layer time + the embedding/LM-head time, measured apart."""
 
-    if threads:
-        torch.set_num_threads(threads)
-    cores = torch.get_num_threads()
-    cfg = LLAMA2_7B
-    shape = LlamaShape.from_hf(cfg)
-    shape.num_layers = 1
-    state = random_native_state(shape, seed=args.seed, dtype=torch.bfloat16)
-    model = OracleModel(shape, state, torch.bfloat16, attention="torch")
-    prompts = make_prompts(args.batch, args.seed, cfg["vocab_size"])
-    prompt = prompts[0][:512]
-    steps = 3
-    t0 = time.perf_counter()
-    first, cache, _ = model.prefill(prompt, steps + 1)
-    t1 = time.perf_counter()
-    model.decode(first, cache, len(prompt), steps + 1)
-    t2 = time.perf_counter()
-    # One layer measured; the 7B model has 32 (embedding and LM head are small next to them,
-    # their share is added from one extra LM-head timing).
-    lm = torch.randn(1, cfg["hidden_size"]).bfloat16()
-    w = state["lm_head.weight"]
-    t3 = time.perf_counter()
-    for _ in range(3):
-        torch.nn.functional.linear(lm, w)
-    lm_s = (time.perf_counter() - t3) / 3
-    layer_decode_s = (t2 - t1) / steps - lm_s
-    per_token_s = cfg["num_hidden_layers"] * layer_decode_s + lm_s
-    prefill_s = cfg["num_hidden_layers"] * ((t1 - t0) - lm_s) + lm_s
-    return {"value": round(1.0 / per_token_s, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": (f"oracle (reference algorithm, torch CPU bf16) on 1 of 32 Llama-2-7B layers: "
-                       f"prefill {len(prompt)} tokens + {steps} decode steps at batch 1, extrapolated "
-                       f"to 32 layers + LM head"),
-            "prefill_ms_extrapolated": round(prefill_s * 1e3, 1)}
+    def __init__(self, prompts, out_len, seed, threads=None):
+        from oracle.llama_ref import CacheState as OCache, LlamaShape, OracleModel, RaggedBatch, random_native_state
+        if threads:
+            torch.set_num_threads(threads)
+        self.cores = torch.get_num_threads()
+        cfg = LLAMA2_7B
+        self.layers = cfg["num_hidden_layers"]
+        shape = LlamaShape.from_hf(cfg)
+        shape.num_layers = 1
+        state = random_native_state(shape, seed=seed, dtype=torch.bfloat16)
+        self.model = OracleModel(shape, state, torch.bfloat16, attention="torch")
+        self.lm = state["lm_head.weight"]
+        self.B, self.out_len = len(prompts), out_len
+        caches, lens, firsts = [], [], []
+        t0 = time.perf_counter()
+        for p in prompts:
+            st = OCache(len(p) + out_len)
+            logits = self.model.forward(torch.tensor([p]), st, last_token_only=True)
+            firsts.append(int(logits.argmax(-1)))
+            caches.append(st.key_value_memory_dict)
+            lens.append(len(p))
+        self.prefill_1layer_s = time.perf_counter() - t0
+        self.batch = RaggedBatch(self.model, caches, lens)
+        self.tokens = torch.tensor(firsts, dtype=torch.long)
+        # LM head share of a step (it does not scale with the layer count).
+        x = torch.randn(self.B, cfg["hidden_size"]).bfloat16()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            torch.nn.functional.linear(x, self.lm)
+        self.head_s = (time.perf_counter() - t0) / 3
+        x1 = torch.randn(1, cfg["hidden_size"]).bfloat16()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            torch.nn.functional.linear(x1, self.lm)
+        self.head1_s = (time.perf_counter() - t0) / 3
+        self.step_s = []
+
+    def step(self):
+        t0 = time.perf_counter()
+        logits = self.batch.step(self.tokens)
+        self.tokens = logits.argmax(-1)
+        self.step_s.append(time.perf_counter() - t0)
+
+    def result(self, kind="port") -> dict:
+        dec1 = statistics.median(self.step_s)
+        dec_full = self.layers * (dec1 - self.head_s) + self.head_s
+        pre_full = self.layers * (self.prefill_1layer_s - self.B * self.head1_s) + self.B * self.head1_s
+        job_s = pre_full + (self.out_len - 1) * dec_full
+        return {"value": round(self.B * self.out_len / job_s, 3), "unit": "tokens/s",
+                "cores": self.cores, "kind": kind,
+                "decode_phase_tokens_per_s": round(self.B / dec_full, 3),
+                "prefill_s_extrapolated": round(pre_full, 2),
+                "decode_step_s_extrapolated": round(dec_full, 4),
+                "sample_step_ms": round(dec1 * 1e3, 2),
+                "sample": (f"oracle (reference algorithm, torch CPU bf16, {self.cores} threads) on 1 of "
+                           f"{self.layers} Llama-2-7B layers + embedding/LM head: the bench's {self.B} "
+                           f"prompts prefilled one by one (batch 1), then {len(self.step_s)} decode steps "
+                           f"of the ragged batch of {self.B}; extrapolated to {self.layers} layers and "
+                           f"{self.out_len} output tokens (generated tokens / (prefill + "
+                           f"{self.out_len - 1} decode steps))")}
+
+
+def host_info() -> dict:
+    info = {"os_cpu_count": os.cpu_count(), "affinity": len(os.sched_getaffinity(0)),
+            "torch_threads": torch.get_num_threads()}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.startswith(("Model name", "Socket(s)", "Core(s) per socket", "Thread(s) per core")):
+                k, v = line.split(":", 1)
+                info[k.strip()] = v.strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return info
+
+
+def cpu_baseline(args, prompts, out_len, threads=None) -> dict:
+    sample = CpuSample(prompts, out_len, args.seed, threads=threads)
+    for _ in range(2):
+        sample.step()
+    res = sample.result()
+    res["host"] = host_info()
+    return res
 
 
 def run_reference(args) -> dict:
+    """--impl reference: the reference algorithm on the host cores, same metric and workload
+    (BASELINE config 3 at batch 32), every host thread. Each timed step is one ragged decode
+    step of the one-layer sample; the line's value extrapolates to the full model and the full
+    job (prefill + 255 decode steps), like cpu_baseline."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    threads = os.cpu_count() or 1
-    cpu = cpu_baseline(args, threads=threads)
+    threads = len(os.sched_getaffinity(0)) or os.cpu_count() or 1
+    prompts = make_prompts(args.batch, args.seed, LLAMA2_7B["vocab_size"])
+    sample = CpuSample(prompts, args.out_len, args.seed, threads=threads)
+    for _ in range(args.warmup):
+        sample.step()
+    sample.step_s.clear()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sample.step()
+    wall = time.perf_counter() - t0
+    cpu = sample.result()
+    cpu["host"] = host_info()
+    lens = [len(p) for p in prompts]
     return {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(wall * 1e3 / max(1, args.steps), 2),
+            "ms_per_step_is": "one timed sample step (one layer of the ragged batch-32 decode step)",
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "Llama-2-7B arch (BASELINE config 3), CPU sample",
-                       "model": "llama-2-7b-arch", "batch": 1},
+            "data": "synthetic (random-init weights, uniform token ids, lognormal prompt lengths)",
+            "impl": "reference", "value_definition": VALUE_DEFINITION,
+            "config": {"workload": "Llama-2-7B arch (BASELINE config 3), host CPU, one layer timed and extrapolated",
+                       "model": "llama-2-7b-arch", "batch": args.batch,
+                       "prompt_lens_mean": round(sum(lens) / len(lens), 1), "output_len": args.out_len,
+                       "parallelism": "host CPU threads"},
             "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -557,11 +727,24 @@ def main():
                          "B,hq,hkv,d,S; kv_pack: layers,hkv,d,L,B")
     ap.add_argument("--epi", choices=["none", "residual", "swiglu"], default="none")
     ap.add_argument("--iters", type=int, default=50)
-    ap.add_argument("--workload", choices=["serve", "kv_handoff", "continuous"], default="serve",
-                    help="kv_handoff: the KV-cache handoff microbenchmark (70B cache geometry); "
-                         "continuous: continuous batching under Poisson arrivals (one GPU)")
-    ap.add_argument("--requests", type=int, default=64, help="continuous: number of requests")
-    ap.add_argument("--rate", type=float, default=8.0, help="continuous: arrivals per second")
+    ap.add_argument("--workload", choices=["serve", "llama70b", "kv_handoff", "continuous", "peer_copy"],
+                    default="serve",
+                    help="serve: BASELINE config 3 (Llama-2-7B), colocated at N=1, disaggregated at "
+                         "N>1; llama70b: config 4 (Llama-2-70B, prefill TP=N/2 -> decode TP=N/2, "
+                         "Poisson arrivals); kv_handoff: config 5 KV-cache handoff microbenchmark; "
+                         "continuous: continuous batching under Poisson arrivals on one GPU; "
+                         "peer_copy: NVLink peer-copy GB/s between GPU 0 and 1")
+    ap.add_argument("--split", default="",
+                    help="N>1 serve: 'P:tp' = P prefill GPUs, tensor-parallel groups of tp "
+                         "(default: about one prefill GPU per three decode GPUs, TP1)")
+    ap.add_argument("--ring-gb", type=float, default=0.0,
+                    help="N>1: staging ring per decode rank in GiB (default: sized from the workload)")
+    ap.add_argument("--kv-bidir", action="store_true",
+                    help="kv_handoff: every GPU sends to (r + N/2) mod N and receives at once")
+    ap.add_argument("--requests", type=int, default=64,
+                    help="continuous / llama70b: number of requests")
+    ap.add_argument("--rate", type=float, default=8.0,
+                    help="continuous / llama70b: Poisson arrivals per second")
     ap.add_argument("--kv-batches", default="1,8,64",
                     help="kv_handoff: requests per transfer, comma separated")
     ap.add_argument("--ragged", action="store_true",
@@ -571,6 +754,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (small ncu captures / tests only; 0 = the model's own)")
     ap.add_argument("--out-len", type=int, default=256)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=1)
@@ -585,18 +770,21 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.kernel:
         line = run_kernel(args)
+    elif args.workload == "peer_copy":
+        import bench_disagg
+        line = bench_disagg.run_peer_copy(args)
     elif args.workload == "continuous" and args.impl == "native":
         line = run_continuous(args)
     elif args.workload == "kv_handoff" and args.impl == "native":
-        from hexgen2_b200.disagg import run_kv_bench
-        line = run_kv_bench(args, sys.modules[__name__])
+        import bench_disagg
+        line = bench_disagg.run_kv_bench(args, sys.modules[__name__])
     elif args.impl == "reference":
         line = run_reference(args)
-    elif args.gpus == 1:
+    elif args.gpus == 1 and args.workload == "serve":
         line = run_native_single(args)
     else:
-        from hexgen2_b200.disagg import run_bench_disaggregated
-        line = run_bench_disaggregated(args, sys.modules[__name__])
+        import bench_disagg
+        line = bench_disagg.run_serving(args, sys.modules[__name__])
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -216,7 +216,6 @@ class Engine:
         tokens[0] = first_tokens.reshape(B)
         if steps <= 0:
             return tokens.t()
-        profiling = ops.PROFILE is not None
 
         def graph_key():
             cos = self.model.rope_tables(capacity, self.device, self.dtype)[0]
@@ -224,7 +223,7 @@ class Engine:
                     cos.data_ptr())
 
         graphs = self.__dict__.setdefault("_decode_graphs", {})
-        entry = None if (profiling or not use_graph) else graphs.get(graph_key())
+        entry = graphs.get(graph_key()) if use_graph else None
         if entry is None:
             state = CacheState(capacity, max_batch_size=B)
             state.key_value_memory_dict = caches
@@ -239,35 +238,23 @@ class Engine:
             lengths.add_(1)
             cur.view(B).copy_(nxt)
 
-        captured = []  # per-kernel event pairs recorded as graph nodes (profiling only)
         for s in range(steps):
             if entry is not None:
                 graph.replay()
                 ops.LAUNCHES += per_replay  # kernels of this library inside one replay
-            elif use_graph and (s >= 1 or (capture_first and not profiling)) and (
-                    steps - s > 1 or not profiling):
+            elif use_graph and (s >= 1 or capture_first):
                 graph = torch.cuda.CUDAGraph()
                 before = ops.LAUNCHES
-                mark = len(ops.PROFILE) if profiling else 0
                 with torch.cuda.graph(graph):
                     step()
                 per_replay = ops.LAUNCHES - before  # counted once at capture = first replay
-                if profiling:
-                    captured = ops.PROFILE[mark:]
-                    del ops.PROFILE[mark:]
                 entry = (graph, cur, per_replay)
-                if not profiling:
-                    if len(graphs) >= 4:
-                        graphs.pop(next(iter(graphs)))
-                    graphs[graph_key()] = entry
+                if len(graphs) >= 4:
+                    graphs.pop(next(iter(graphs)))
+                graphs[graph_key()] = entry
                 graph.replay()
             else:
                 step()
-            if captured:
-                # Profiling: read this replay's kernel timestamps before the next replay
-                # overwrites them.
-                torch.cuda.synchronize()
-                ops.PROFILE.extend(ops.profile_durations(captured))
             tokens[s + 1].copy_(cur.view(B))
         return tokens.t()
 
@@ -363,6 +350,38 @@ class ContinuousBatcher:
         if self.left[slot] == 0:
             self._retire(slot)
         return first
+
+    @torch.inference_mode()
+    def admit_packed(self, req_id, src, src_offset: int, length: int, first_token: int,
+                     max_new_tokens: int) -> int:
+        """Admits a request prefilled elsewhere into a free slot: its live rows of every layer,
+        packed as Engine.pack_live and the prefill rank's gather-pack write them ([layers][L]
+        rows of [2, hkv, d] at byte offset src_offset of `src`, a CUDA tensor or a device
+        address on this GPU), are scattered into the slot with one kernel, and decoding
+        continues from first_token. Returns the slot."""
+        free = self.free_slots()
+        if not free:
+            raise ValueError("no free slot")
+        if length + max_new_tokens > self.capacity:
+            raise ValueError(f"request needs {length + max_new_tokens} positions, capacity {self.capacity}")
+        slot = free[0]
+        dev = self.eng.device
+        big0 = self.cache[0]
+        elem = big0.element_size()
+        n = self.eng.num_layers
+        layer_stride = self.cache[1].data_ptr() - big0.data_ptr() if n > 1 else 0
+        dst = torch.tensor([big0.data_ptr() + slot * big0.stride(0) * elem], dtype=torch.int64,
+                           device=dev)
+        ops.kv_unpack(src, torch.tensor([src_offset], dtype=torch.int64, device=dev),
+                      torch.tensor([length], dtype=torch.int64, device=dev), dst, n, layer_stride,
+                      big0.stride(1) * elem, self.eng.row_bytes, length)
+        self.tokens[slot:slot + 1].fill_(first_token)
+        self.lengths[slot:slot + 1].fill_(length)
+        self.req[slot], self.left[slot] = req_id, max_new_tokens - 1
+        self.out[req_id] = [first_token]
+        if self.left[slot] == 0:
+            self._retire(slot)
+        return slot
 
     def _retire(self, slot: int):
         self.req[slot] = None

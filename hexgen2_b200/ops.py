@@ -41,41 +41,17 @@ def _require_cuda(*ts):
 
 _workspaces: dict[int, torch.Tensor] = {}
 
-# Instrumentation used by bench.py: LAUNCHES counts kernels launched through this module;
-# when PROFILE is a list, every op appends (name, start_event, end_event) recorded on the
-# launching stream.
+# Number of kernels launched through this module (bench.py reports it as gpu_launches; a CUDA
+# graph replay adds the launches it captured).
 LAUNCHES = 0
-PROFILE: list | None = None
 # Bumped whenever a scratch buffer is reallocated: CUDA graphs that captured the old address
 # must not be replayed.
 WORKSPACE_GEN = 0
 
 
-def _begin(name):
-    if PROFILE is None:
-        return None
-    # external=True: inside a CUDA-graph capture the record becomes an event-record node, so a
-    # replayed graph still timestamps every kernel.
-    e = torch.cuda.Event(enable_timing=True, external=True)
-    e.record()
-    return name, e
-
-
-def _end(tok, launches=1):
+def _count(launches=1):
     global LAUNCHES
     LAUNCHES += launches
-    if tok is not None:
-        e = torch.cuda.Event(enable_timing=True, external=True)
-        e.record()
-        PROFILE.append((tok[0], tok[1], e))
-
-
-def profile_durations(entries) -> list:
-    """[(name, ms)] for PROFILE entries (event pairs must have completed)."""
-    out = []
-    for ent in entries:
-        out.append((ent[0], ent[1]) if len(ent) == 2 else (ent[0], ent[1].elapsed_time(ent[2])))
-    return out
 
 
 def workspace(nbytes: int, device=None, kind: str = "attn") -> torch.Tensor | None:
@@ -106,21 +82,19 @@ def rmsnorm(x, weight, eps, add=None, residual_out=None, out=None, rows=None, in
         in_stride = x.stride(-2) if x.dim() >= 2 else hidden
     if out is None:
         out = torch.empty(rows, hidden, dtype=x.dtype, device=x.device)
-    _tok = _begin("rmsnorm")
     check(_L().hx_rmsnorm(_p(x), _p(add), _p(residual_out), _p(out), _p(weight), rows, hidden,
                           in_stride, out.stride(-2) if out.dim() >= 2 else hidden, float(eps),
                           _code(x), _stream()), "hx_rmsnorm")
-    _end(_tok, 1)
+    _count(1)
     return out
 
 
 def embed_rmsnorm(ids, table, weight, eps, residual_out, normed_out):
     _require_cuda(ids, table)
-    _tok = _begin("embed_rmsnorm")
     check(_L().hx_embed_rmsnorm(_p(ids), ids.numel(), _p(table), table.shape[1], _p(weight),
                                 float(eps), _p(residual_out), _p(normed_out), _code(table),
                                 _stream()), "hx_embed_rmsnorm")
-    _end(_tok, 1)
+    _count(1)
 
 
 def embedding(ids, table, vocab_start=0, out=None):
@@ -128,10 +102,9 @@ def embedding(ids, table, vocab_start=0, out=None):
     hidden = table.shape[1]
     if out is None:
         out = torch.empty(ids.numel(), hidden, dtype=table.dtype, device=table.device)
-    _tok = _begin("embedding")
     check(_L().hx_embedding(_p(ids), ids.numel(), _p(table), vocab_start, table.shape[0], hidden,
                             _p(out), _code(table), _stream()), "hx_embedding")
-    _end(_tok, 1)
+    _count(1)
     return out
 
 
@@ -143,14 +116,13 @@ def rotary_cache_write(qkv, batch, seqlen, n_heads, n_heads_kv, head_dim, pos_st
     if q_out is None:
         q_out = torch.empty(batch, seqlen, n_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
     assert cache.stride(-1) == 1 and cache.stride(-2) == head_dim and cache.stride(-3) == n_heads_kv * head_dim
-    _tok = _begin("rotary_cache_write")
     check(_L().hx_rotary_cache_write(_p(qkv), batch, seqlen, n_heads, n_heads_kv, head_dim,
                                      _p(pos_start), _p(cos), _p(sin), cos.shape[0],
                                      1 if interleaved else 0, _p(q_out), _p(cache),
                                      cache.stride(0), cache.stride(1), batch_offset,
                                      cache.shape[1], _code(qkv), _stream()),
           "hx_rotary_cache_write")
-    _end(_tok, 1)
+    _count(1)
     return q_out
 
 
@@ -168,11 +140,10 @@ def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None):
     code = _code(a)
     nbytes = _L().hx_gemm_workspace(M, N, K, epilogue, code)
     ws = workspace(nbytes, kind="gemm" if code != _lib.HX_F32 else "attn")
-    _tok = _begin(f"gemm_decode[{N}x{K}]" if M <= 64 else "gemm_prefill")
     check(_L().hx_gemm(_p(a), _p(w), _p(out), M, N, K, a.stride(0), w.stride(0), out.stride(0),
                        epilogue, _p(residual), residual.stride(0) if residual is not None else 0,
                        _p(ws), nbytes, code, _stream()), "hx_gemm")
-    _end(_tok, 2 if nbytes else 1)
+    _count(2 if nbytes else 1)
     return out
 
 
@@ -188,13 +159,12 @@ def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, 
     code = _code(x)
     nbytes = _L().hx_gemm_workspace(M, N, K, _lib.HX_EPI_QKV_ROTARY, code)
     ws = workspace(nbytes, kind="gemm")
-    _tok = _begin(f"gemm_decode[{N}x{K}]" if M <= 64 else "gemm_prefill")
     check(_L().hx_gemm_qkv_rotary(_p(x), _p(w_qkv), M, K, x.stride(0), seqlen, n_heads,
                                   n_heads_kv, head_dim, _p(pos_start), _p(cos), _p(sin),
                                   cos.shape[0], _p(q_out), _p(cache), cache.stride(0),
                                   cache.stride(1), batch_offset, cache.shape[1], _p(ws), nbytes,
                                   code, _stream()), "hx_gemm_qkv_rotary")
-    _end(_tok, 2 if (nbytes and M > 64) else 1)
+    _count(2 if (nbytes and M > 64) else 1)
     return q_out
 
 
@@ -210,12 +180,11 @@ def prefill_attention(q, cache, pos_start, n_heads_kv, softmax_scale, causal=Tru
     B, S, hq, d = q.shape
     if out is None:
         out = torch.empty_like(q)
-    _tok = _begin("prefill_attention")
     check(_L().hx_prefill_attention(_p(q), _p(cache), cache.stride(0), cache.stride(1),
                                     batch_offset, _p(pos_start), B, S, hq, n_heads_kv, d,
                                     1 if causal else 0, float(softmax_scale), _p(out), _code(q),
                                     _stream()), "hx_prefill_attention")
-    _end(_tok, 1)
+    _count(1)
     return out
 
 
@@ -227,12 +196,11 @@ def decode_attention(q, cache, seqlens, n_heads_kv, max_seqlen, softmax_scale, o
         out = torch.empty(B, hq, d, dtype=q.dtype, device=q.device)
     nbytes = _L().hx_decode_attention_workspace(B, hq, d, max_seqlen)
     ws = workspace(nbytes)
-    _tok = _begin("decode_attention")
     check(_L().hx_decode_attention(_p(q), _p(cache), cache.stride(0), cache.stride(1),
                                    _p(seqlens), B, hq, n_heads_kv, d, max_seqlen,
                                    float(softmax_scale), _p(out), _p(ws), nbytes, _code(q),
                                    _stream()), "hx_decode_attention")
-    _end(_tok, 2 if nbytes else 1)
+    _count(2 if nbytes else 1)
     return out
 
 
@@ -246,10 +214,9 @@ def argmax(logits, out=None):
     rows, cols = logits.shape
     if out is None:
         out = torch.empty(rows, dtype=torch.long, device=logits.device)
-    _tok = _begin("argmax")
     check(_L().hx_argmax(_p(logits), rows, cols, logits.stride(0), _p(out), _code(logits),
                          _stream()), "hx_argmax")
-    _end(_tok, 1)
+    _count(1)
     return out
 
 
@@ -259,21 +226,19 @@ def kv_pack(src_ptrs, live_rows, dst_offsets, n_outer, outer_stride_bytes, row_s
     """Gather-pack of live rows (see hx_kv_pack). Pointer/length/offset arrays are int64 CUDA
     tensors; dst may be a peer GPU's buffer given as a raw address (int)."""
     dst_ptr = dst if isinstance(dst, int) else dst.data_ptr()
-    _tok = _begin("kv_pack")
     check(_L().hx_kv_pack(_p(src_ptrs), _p(live_rows), _p(dst_offsets), src_ptrs.numel(),
                           n_outer, outer_stride_bytes, row_stride_bytes, row_bytes,
                           max_live_rows, dst_ptr, _stream()), "hx_kv_pack")
-    _end(_tok, 1)
+    _count(1)
 
 
 def kv_unpack(src, src_offsets, live_rows, dst_ptrs, n_outer, outer_stride_bytes,
               row_stride_bytes, row_bytes, max_live_rows):
     src_ptr = src if isinstance(src, int) else src.data_ptr()
-    _tok = _begin("kv_unpack")
     check(_L().hx_kv_unpack(src_ptr, _p(src_offsets), _p(live_rows), _p(dst_ptrs),
                             dst_ptrs.numel(), n_outer, outer_stride_bytes, row_stride_bytes,
                             row_bytes, max_live_rows, _stream()), "hx_kv_unpack")
-    _end(_tok, 1)
+    _count(1)
 
 
 def device_error(clear=True) -> int:

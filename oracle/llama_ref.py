@@ -319,6 +319,52 @@ class OracleModel:
         return (generated, all_logits) if return_logits else generated
 
 
+class RaggedBatch:
+    """Batched decode of requests with their own live lengths, for timing the reference
+    algorithm on the host at a serving batch. The reference's Engine decodes one request at a
+    time (model.py:85-121) and its legacy batching pads every cache to the longest
+    (kv_cache_batch.py:4-29); here each request keeps its own cache and length, the projections
+    run once for all B rows (F.linear over [B, h]) and attention runs per request over its own
+    live rows, so the arithmetic is the reference's per-request decode step with the weight
+    reads shared across the batch. Used only as the CPU baseline, never as a checker."""
+
+    def __init__(self, model: OracleModel, caches: list[dict], lengths: list[int]):
+        self.m, self.caches, self.lengths = model, caches, list(lengths)
+
+    @torch.inference_mode()
+    def step(self, tokens: torch.Tensor) -> torch.Tensor:
+        """tokens [B] int64 -> logits [B, V]; every cache grows by one row."""
+        m, sh, w, eps = self.m, self.m.shape, self.m.w, self.m.shape.rms_norm_eps
+        d, hq, hk = sh.head_dim, sh.num_heads, sh.num_kv_heads
+        B = tokens.numel()
+        hidden = F.embedding(tokens.view(B, 1), w["transformer.embeddings.word_embeddings.weight"])
+        residual = None
+        for i in range(sh.num_layers):
+            p = f"transformer.layers.{i}."
+            residual = hidden + residual if residual is not None else hidden
+            x = rms_norm(residual, w[p + "norm1.weight"], eps)
+            qkv = F.linear(x, w[p + "mixer.Wqkv.weight"])  # [B, 1, (hq + 2hk) d]
+            ctx = torch.empty(B, 1, hq * d, dtype=m.dtype)
+            for b in range(B):
+                L = self.lengths[b]
+                q = qkv[b:b + 1, :, : hq * d].reshape(1, 1, hq, d)
+                kv = qkv[b:b + 1, :, hq * d:].reshape(1, 1, 2, hk, d)
+                q = m.rotary.apply(q, L, m.dtype)
+                k = m.rotary.apply(kv[:, :, 0], L, m.dtype)
+                cache = self.caches[b][i]
+                cache[:, L, 0] = k[:, 0]
+                cache[:, L, 1] = kv[:, 0, 1]
+                ctx[b] = m._attn(q, cache[:, :L + 1], False).reshape(1, hq * d)
+            hidden = F.linear(ctx, w[p + "mixer.out_proj.weight"])
+            residual = hidden + residual
+            x = rms_norm(residual, w[p + "norm2.weight"], eps)
+            hidden = m._mlp(x, i)
+        residual = hidden + residual
+        x = rms_norm(residual, w["transformer.ln_f.weight"], eps)
+        self.lengths = [L + 1 for L in self.lengths]
+        return F.linear(x[:, -1], w["lm_head.weight"])
+
+
 def load_hf_checkpoint(folder, dtype=torch.float32):
     """Reads a HF Llama safetensors checkpoint: (LlamaShape, native state dict)."""
     import json

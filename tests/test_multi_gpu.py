@@ -4,9 +4,12 @@ skipped on a single-GPU box.
 * The KV handoff moves bytes exactly: rank 0's gather-pack kernel writes the live rows of a
   seeded random cache straight into rank 1's IPC-mapped buffer; rank 1 regenerates the same
   cache and packs it locally; the two buffers are compared byte for byte.
-* Disaggregated serving equals colocated serving: prompts prefilled on rank 0, KV handed to
-  rank 1 over NVLink, ragged batch decoded there == the same batch served colocated on rank 1
-  (greedy tokens identical). With 4 GPUs the same runs with tensor parallelism 2 per group.
+* Streaming disaggregated serving equals colocated serving: requests prefilled on the prefill
+  group, their KV streamed one at a time over NVLink into the decode group's continuous
+  batcher, tokens identical to the decode engine's own prefill + greedy decode. Splits 1 -> 1
+  (2 GPUs), 1 -> 3 and TP2 -> TP2 (4 GPUs).
+* Mismatched-TP KV re-shard with shards on two GPUs of one process equals the reference's
+  head concat.
 """
 import os
 import socket
@@ -90,26 +93,92 @@ def _handoff_worker(rank, world, port, errors):
         raise
 
 
-def _serve_worker(rank, world, port, errors):
+def _serve_worker(rank, world, port, errors, split_args=(1, 1)):
+    """Streams requests of varied prompt and output lengths through the disaggregated pipeline
+    (hexgen2_b200.serving) twice and checks, on every decode rank, that each request's tokens
+    equal the same engine's own colocated prefill + greedy decode of that request."""
     try:
+        import time
         _init(rank, world, port)
-        from hexgen2_b200.disagg import DisaggregatedPair
+        from hexgen2_b200.engine import Engine
+        from hexgen2_b200.serving import (DecodeWorker, PrefillWorker, Request, Split, assign,
+                                          connect_rings, make_groups)
+        split = Split(world, *split_args)
+        group = make_groups(split)
+        kind, j, t = split.role(rank)
+        eng = Engine.from_config(SMALL, dtype="bfloat16", seed=3, process_group=group)
         g = torch.Generator().manual_seed(5)
-        prompts = [torch.randint(0, SMALL["vocab_size"], (L,), generator=g).tolist()
-                   for L in (17, 130, 3, 64)]
-        out_len = 9
-        pair = DisaggregatedPair(SMALL, prompts, out_len, seed=3)
-        if pair.is_prefill:
-            pair.prefill_all(False)
+        shapes = [(17, 9), (130, 4), (3, 12), (64, 1), (40, 7), (90, 10), (8, 5), (200, 3)]
+        reqs = assign([Request(i, torch.randint(0, SMALL["vocab_size"], (L,), generator=g).tolist(), n)
+                       for i, (L, n) in enumerate(shapes)], split)
+        store = dist.PrefixStore("test-serve", dist.distributed_c10d._get_default_store())
+        ring = 3 * 210 * eng.num_layers * eng.row_bytes  # small ring: regions wrap and wait
+        handoffs, staging, remotes = connect_rings(split, ring)
+        if kind == "prefill":
+            worker = PrefillWorker(eng, split, store, remotes, ring, max_prompt=210)
+            for rnd in range(2):  # a second run reuses the rings and the kept graphs
+                dist.barrier()
+                worker.run(reqs, f"r{rnd}", time.monotonic())
+                dist.barrier()
         else:
-            toks, _, _ = pair.decode_all(False, use_graph=True)
-            got = toks.cpu().tolist()
-            ref = pair.eng.serve_batch(prompts, max_new_tokens=out_len)
-            assert got == ref, (got, ref)
+            worker = DecodeWorker(eng, split, store, staging, slots=3, capacity=220)
+            for rnd in range(2):
+                dist.barrier()
+                got = worker.run(reqs, f"r{rnd}", time.monotonic())
+                dist.barrier()
+                mine = [r for r in reqs if r.group == j]
+                assert set(got) == {r.rid for r in mine}
+                for r in mine:
+                    first, cache, _ = eng.prefill(r.prompt, r.max_new)
+                    ref = eng.decode(first, cache, len(r.prompt), r.max_new)
+                    assert got[r.rid] == ref, (rnd, r.rid, got[r.rid], ref)
         torch.cuda.synchronize()
         dist.barrier()
-        pair.close()
+        for h in handoffs:
+            h.close()
+        if kind == "decode":
+            eng.release_graphs()
+        dist.barrier()
         dist.destroy_process_group()
+    except Exception as e:
+        errors.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def _serve_1_3(rank, world, port, errors):
+    _serve_worker(rank, world, port, errors, (1, 1))
+
+
+def _serve_tp2(rank, world, port, errors):
+    _serve_worker(rank, world, port, errors, (2, 2))
+
+
+def _reshard_two_devices(rank, world, port, errors):
+    """Mismatched-TP re-shard with the shards on two GPUs of ONE process: packs run on the
+    source's device, unpacks on the destination's (rank 0 does it all; rank 1 does nothing)."""
+    try:
+        if rank == 0:
+            from oracle.llama_ref import concat_kv_heads
+            from hexgen2_b200.transport import reshard_kv
+            layers, B, cap, H, d = 2, 2, 40, 4, 64
+            lens, rows = [33, 7], [1, 0]
+            gen = torch.Generator().manual_seed(8)
+            full = torch.randn(layers, B, cap, 2, H, d, generator=gen).bfloat16()
+            src = []
+            for s in range(2):  # shard s on GPU s
+                shard = full[:, :, :, :, s * 2:(s + 1) * 2].contiguous().to(f"cuda:{s}")
+                src.append({i: shard[i] for i in range(layers)})
+            dst_big = torch.zeros(layers, B, cap, 2, H, d, dtype=torch.bfloat16, device="cuda:1")
+            dst = [{i: dst_big[i] for i in range(layers)}]
+            torch.cuda.set_device(0)  # the current device is not the unpack's
+            reshard_kv(src, dst, rows, lens, H)
+            torch.cuda.synchronize(0)
+            torch.cuda.synchronize(1)
+            for row, L in zip(rows, lens):
+                shards = [{i: src[s][i][row:row + 1, :L].cpu() for i in range(layers)} for s in range(2)]
+                whole = concat_kv_heads(shards)
+                for i in range(layers):
+                    assert torch.equal(dst[0][i][row:row + 1, :L].cpu(), whole[i])
     except Exception as e:
         errors.put(f"rank {rank}: {type(e).__name__}: {e}")
         raise
@@ -144,11 +213,25 @@ def test_kv_handoff_bytes_exact_over_nvlink():
     _run(_handoff_worker, 2)
 
 
-def test_disaggregated_serving_equals_colocated_2gpu():
+def test_streaming_serving_equals_colocated_2gpu():
+    """1 prefill GPU -> 1 decode GPU, requests streamed one at a time through a wrapping ring."""
     _need(2)
     _run(_serve_worker, 2)
 
 
-def test_disaggregated_serving_equals_colocated_tp2():
+def test_streaming_serving_one_prefill_three_decode():
+    """1 prefill GPU feeding 3 decode GPUs (the default split at N = 4)."""
     _need(4)
-    _run(_serve_worker, 4)
+    _run(_serve_1_3, 4)
+
+
+def test_streaming_serving_tp2_to_tp2():
+    """Prefill TP2 -> decode TP2 (BASELINE config 3's split): leader-decided admissions keep
+    the decode group's collectives in step; greedy tokens via one all-reduce of keys."""
+    _need(4)
+    _run(_serve_tp2, 4)
+
+
+def test_reshard_kv_across_two_devices():
+    _need(2)
+    _run(_reshard_two_devices, 2)

@@ -61,3 +61,29 @@ def test_kv_packet_bytes_closed_form(golden):
     for p in golden["transport"]:
         elem = {"float16": 2, "bfloat16": 2, "float32": 4}[p["dtype"]]
         assert p["payload_bytes"] == 8 + 2 * 4 * 2 * 2 * 32 * elem
+
+
+def test_ragged_batch_decode_equals_per_request_decode(fixture_dir):
+    """oracle.RaggedBatch (the CPU baseline's batched decode) gives every request the logits of
+    its own batch-1 decode (model.py:85-121 flow), in f32."""
+    from oracle.llama_ref import CacheState, RaggedBatch
+    shape, state = load_hf_checkpoint(fixture_dir)
+    model = OracleModel(shape, state, torch.float32, attention="torch")
+    prompts = [[5, 9, 2], list(range(1, 20)), [7]]
+    steps = 4
+    caches, lens, firsts, singles = [], [], [], []
+    for p in prompts:
+        st = CacheState(len(p) + steps + 1)
+        logits = model.forward(torch.tensor([p]), st, last_token_only=True)
+        caches.append(st.key_value_memory_dict)
+        lens.append(len(p))
+        firsts.append(int(logits.argmax(-1)))
+        f, c, _ = model.prefill(p, steps + 1)
+        singles.append(model.decode(f, c, len(p), steps + 1, return_logits=True)[1])
+    batch = RaggedBatch(model, caches, lens)
+    tok = torch.tensor(firsts)
+    for s in range(steps):
+        logits = batch.step(tok)
+        for b in range(len(prompts)):
+            torch.testing.assert_close(logits[b], singles[b][s][0], rtol=0, atol=1e-5)
+        tok = logits.argmax(-1)
