@@ -33,20 +33,12 @@ _SIGNATURES = {
     "hx_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                         c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_size_t, c_int,
                         c_void_p]),
-    "hx_gemm_ex": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
-                           c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_size_t, c_int,
-                           c_void_p, c_size_t, c_void_p]),
     "hx_gemm_workspace": (c_size_t, [c_int64, c_int64, c_int64, c_int, c_int]),
     "hx_gemm_kernel_kind": (c_int, [c_int64, c_int64, c_int64, c_int]),
     "hx_gemm_qkv_rotary": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                                    c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
                                    c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                    c_void_p, c_size_t, c_int, c_void_p]),
-    "hx_gemm_qkv_rotary_ex": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
-                                      c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
-                                      c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int64,
-                                      c_int64, c_void_p, c_size_t, c_int, c_void_p, c_size_t,
-                                      c_void_p]),
     "hx_prefill_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
                                      c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_float,
                                      c_void_p, c_int, c_void_p]),

@@ -214,14 +214,6 @@ HX_DEVICE void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
       : "memory");
 }
 
-// Bulk prefetch of [p, p + bytes) into L2 (no destination, no completion tracking). p and
-// bytes must be multiples of 16.
-HX_DEVICE void l2_prefetch_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
-               "r"(bytes)
-               : "memory");
-}
-
 HX_DEVICE void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -58,11 +58,6 @@ struct GemmArgs {
   int64_t ldr;
   float* ws;        // split-K partials [k_splits][M][N] (M > 64 only)
   QkvArgs qkv;
-  // Decode-shaped kernel only: bytes of the NEXT projection's weights to pull into L2 once this
-  // CTA has issued its last weight load (each CTA takes an equal 16-byte-aligned slice), so the
-  // HBM keeps streaming across the kernel boundary (tail, small kernels in between, ramp-up).
-  const uint8_t* pf;
-  uint64_t pf_bytes;
 };
 
 HX_DEVICE float silu_f(float g) { return g / (1.0f + expf(-g)); }
@@ -589,13 +584,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       counters[0] = issued;
-      if (a.pf_bytes) {
-        const uint64_t per = (a.pf_bytes / gridDim.x + 15) & ~uint64_t(15);
-        const uint64_t lo = (uint64_t)blockIdx.x * per;
-        const uint64_t hi = lo + per < a.pf_bytes ? lo + per : a.pf_bytes;
-        for (uint64_t off = lo; off < hi; off += 65536)
-          l2_prefetch_bulk(a.pf + off, (uint32_t)(hi - off < 65536 ? hi - off : 65536));
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -1237,12 +1225,9 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
 template <typename T, int EPI>
 int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int64_t K,
               int64_t lda, int64_t ldb, int64_t ldc, const void* R, int64_t ldr, void* ws,
-              size_t ws_bytes, int dtype, cudaStream_t stream, const QkvArgs* qkv = nullptr,
-              const void* pf = nullptr, size_t pf_bytes = 0) {
+              size_t ws_bytes, int dtype, cudaStream_t stream, const QkvArgs* qkv = nullptr) {
   const Plan p = plan_gemm(M, N, K);
   GemmArgs a;
-  a.pf = static_cast<const uint8_t*>(pf);
-  a.pf_bytes = pf ? (pf_bytes & ~size_t(15)) : 0;
   a.M = (int)M;
   a.N = (int)N;
   a.K = (int)K;
@@ -1363,13 +1348,13 @@ size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtyp
   return plan_workspace(plan_gemm(m, n, k), m, n);
 }
 
-int hx_gemm_qkv_rotary_ex(const void* x, const void* w_qkv, int64_t m, int64_t k, int64_t ldx,
+int hx_gemm_qkv_rotary(const void* x, const void* w_qkv, int64_t m, int64_t k, int64_t ldx,
                        int64_t seqlen, int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
                        const int32_t* pos_start, const void* cos_table, const void* sin_table,
                        int64_t table_rows, void* q_out, void* cache, int64_t cache_batch_stride,
                        int64_t cache_seq_stride, int64_t cache_batch_offset,
                        int64_t cache_max_seq, void* workspace, size_t workspace_bytes, int dtype,
-                       const void* l2_prefetch, size_t l2_prefetch_bytes, void* stream) {
+                       void* stream) {
   HX_REQUIRE(x && w_qkv && pos_start && cos_table && sin_table && q_out && cache,
              "hx_gemm_qkv_rotary: null pointer");
   HX_REQUIRE(dtype == HX_BF16 || dtype == HX_F16, "hx_gemm_qkv_rotary: f16/bf16 only");
@@ -1403,30 +1388,15 @@ int hx_gemm_qkv_rotary_ex(const void* x, const void* w_qkv, int64_t m, int64_t k
   if (dtype == HX_BF16)
     return gemm_half<__nv_bfloat16, HX_EPI_QKV_ROTARY>(x, w_qkv, nullptr, m, n, k, ldx, k, 0,
                                                        nullptr, 0, workspace, workspace_bytes,
-                                                       dtype, s, &q, l2_prefetch, l2_prefetch_bytes);
+                                                       dtype, s, &q);
   return gemm_half<__half, HX_EPI_QKV_ROTARY>(x, w_qkv, nullptr, m, n, k, ldx, k, 0, nullptr, 0,
-                                              workspace, workspace_bytes, dtype, s, &q,
-                                              l2_prefetch, l2_prefetch_bytes);
+                                              workspace, workspace_bytes, dtype, s, &q);
 }
 
-int hx_gemm_qkv_rotary(const void* x, const void* w_qkv, int64_t m, int64_t k, int64_t ldx,
-                       int64_t seqlen, int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
-                       const int32_t* pos_start, const void* cos_table, const void* sin_table,
-                       int64_t table_rows, void* q_out, void* cache, int64_t cache_batch_stride,
-                       int64_t cache_seq_stride, int64_t cache_batch_offset,
-                       int64_t cache_max_seq, void* workspace, size_t workspace_bytes, int dtype,
-                       void* stream) {
-  return hx_gemm_qkv_rotary_ex(x, w_qkv, m, k, ldx, seqlen, n_heads, n_heads_kv, head_dim,
-                               pos_start, cos_table, sin_table, table_rows, q_out, cache,
-                               cache_batch_stride, cache_seq_stride, cache_batch_offset,
-                               cache_max_seq, workspace, workspace_bytes, dtype, nullptr, 0,
-                               stream);
-}
-
-int hx_gemm_ex(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
-               int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
-               int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
-               const void* l2_prefetch, size_t l2_prefetch_bytes, void* stream) {
+int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
+            int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
+            int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
+            void* stream) {
   HX_REQUIRE(epilogue != HX_EPI_QKV_ROTARY, "hx_gemm: use hx_gemm_qkv_rotary for that epilogue");
   HX_REQUIRE(a && b && c && m >= 0 && n >= 0 && k > 0, "hx_gemm: bad arguments");
   HX_REQUIRE(lda >= k && ldb >= k, "hx_gemm: lda/ldb smaller than k");
@@ -1447,16 +1417,13 @@ int hx_gemm_ex(const void* a, const void* b, void* c, int64_t m, int64_t n, int6
   switch (epilogue) {                                                                         \
     case HX_EPI_NONE:                                                                         \
       return gemm_half<T, HX_EPI_NONE>(a, b, c, m, n, k, lda, ldb, ldc, residual, ld_residual, \
-                                       workspace, workspace_bytes, dtype, s, nullptr,          \
-                                       l2_prefetch, l2_prefetch_bytes);       \
+                                       workspace, workspace_bytes, dtype, s);                 \
     case HX_EPI_RESIDUAL:                                                                     \
       return gemm_half<T, HX_EPI_RESIDUAL>(a, b, c, m, n, k, lda, ldb, ldc, residual,         \
-                                           ld_residual, workspace, workspace_bytes, dtype, s,  \
-                                           nullptr, l2_prefetch, l2_prefetch_bytes); \
+                                           ld_residual, workspace, workspace_bytes, dtype, s); \
     default:                                                                                  \
       return gemm_half<T, HX_EPI_SWIGLU>(a, b, c, m, n, k, lda, ldb, ldc, residual,           \
-                                         ld_residual, workspace, workspace_bytes, dtype, s,   \
-                                         nullptr, l2_prefetch, l2_prefetch_bytes);  \
+                                         ld_residual, workspace, workspace_bytes, dtype, s);  \
   }
   if (dtype == HX_BF16) {
     HX_GEMM_EPI(__nv_bfloat16)
@@ -1465,14 +1432,6 @@ int hx_gemm_ex(const void* a, const void* b, void* c, int64_t m, int64_t n, int6
   }
 #undef HX_GEMM_EPI
   return HX_OK;
-}
-
-int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
-            int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
-            int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
-            void* stream) {
-  return hx_gemm_ex(a, b, c, m, n, k, lda, ldb, ldc, epilogue, residual, ld_residual, workspace,
-                    workspace_bytes, dtype, nullptr, 0, stream);
 }
 
 }  // extern "C"

@@ -340,14 +340,9 @@ class GPTLMHeadModel(nn.Module):
             emb = self.transformer.embeddings(ids.view(B, S)).view(rows, h)
             ops.rmsnorm(emb, layers[0].norm1.weight, self.eps, residual_out=residual, out=normed)
         seqlens = pos + 1 if decode else None
-        # Decode-shaped projections (<= 64 rows) pull the next projection's first weight bytes
-        # into L2 as they finish, so HBM streams across the small kernels in between.
-        small = rows <= 64
         for i, layer in enumerate(layers):
             mixer, mlp = layer.mixer, layer.mlp
             cache = caches[i]
-            nxt_qkv = (layers[i + 1].mixer.Wqkv.weight if i + 1 < len(layers)
-                       else self.lm_head.weight) if small else None
             if dtype != torch.float32 and mixer.rotary_emb_interleaved:
                 q = ops.gemm_qkv_rotary(normed, mixer.Wqkv.weight, S, hq, hk, d, pos, cos, sin,
                                         cache, batch_offset=b0).view(B, S, hq, d)
@@ -365,24 +360,21 @@ class GPTLMHeadModel(nn.Module):
                                             batch_offset=b0)
             ctx = ctx.view(rows, hq * d)
             if self.tp == 1:
-                ops.gemm(ctx, mixer.out_proj.weight, HX_EPI_RESIDUAL, residual=residual, out=residual,
-                         prefetch=mlp.fc1.weight if small else None)
+                ops.gemm(ctx, mixer.out_proj.weight, HX_EPI_RESIDUAL, residual=residual, out=residual)
                 ops.rmsnorm(residual, layer.norm2.weight, self.eps, out=normed)
             else:
-                part = ops.gemm(ctx, mixer.out_proj.weight, prefetch=mlp.fc1.weight if small else None)
+                part = ops.gemm(ctx, mixer.out_proj.weight)
                 self._all_reduce(part)
                 ops.rmsnorm(part, layer.norm2.weight, self.eps, add=residual,
                             residual_out=residual, out=normed)
-            act = ops.gemm(normed, mlp.fc1.weight, HX_EPI_SWIGLU,
-                           prefetch=mlp.fc2.weight if small else None)
+            act = ops.gemm(normed, mlp.fc1.weight, HX_EPI_SWIGLU)
             nxt = layers[i + 1].norm1.weight if i + 1 < len(layers) else None
             if self.tp == 1:
-                ops.gemm(act, mlp.fc2.weight, HX_EPI_RESIDUAL, residual=residual, out=residual,
-                         prefetch=nxt_qkv)
+                ops.gemm(act, mlp.fc2.weight, HX_EPI_RESIDUAL, residual=residual, out=residual)
                 if nxt is not None:
                     ops.rmsnorm(residual, nxt, self.eps, out=normed)
             else:
-                part = ops.gemm(act, mlp.fc2.weight, prefetch=nxt_qkv)
+                part = ops.gemm(act, mlp.fc2.weight)
                 self._all_reduce(part)
                 if nxt is not None:
                     ops.rmsnorm(part, nxt, self.eps, add=residual, residual_out=residual, out=normed)

@@ -127,19 +127,8 @@ def rotary_cache_write(qkv, batch, seqlen, n_heads, n_heads_kv, head_dim, pos_st
 
 
 # ----------------------------------------------------------------------------- gemm
-# Bytes of the next projection's weights a decode-shaped GEMM pulls into L2 (hx_gemm_ex).
-L2_PREFETCH_BYTES = 32 << 20
-
-
-def _prefetch_args(prefetch):
-    if prefetch is None:
-        return None, 0
-    return prefetch.data_ptr(), min(prefetch.numel() * prefetch.element_size(), L2_PREFETCH_BYTES)
-
-
-def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None, prefetch=None):
-    """out = a @ w.T with an epilogue; a [M, K] (row-strided), w [N, K]. prefetch: the weight
-    of the projection that follows (decode-shaped calls pull its first bytes into L2)."""
+def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None):
+    """out = a @ w.T with an epilogue; a [M, K] (row-strided), w [N, K]."""
     _require_cuda(a, w, residual)
     M, K = a.shape
     N = w.shape[0]
@@ -151,16 +140,15 @@ def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None, prefetch=None):
     code = _code(a)
     nbytes = _L().hx_gemm_workspace(M, N, K, epilogue, code)
     ws = workspace(nbytes, kind="gemm" if code != _lib.HX_F32 else "attn")
-    pf, pf_bytes = _prefetch_args(prefetch)
-    check(_L().hx_gemm_ex(_p(a), _p(w), _p(out), M, N, K, a.stride(0), w.stride(0), out.stride(0),
-                          epilogue, _p(residual), residual.stride(0) if residual is not None else 0,
-                          _p(ws), nbytes, code, pf, pf_bytes, _stream()), "hx_gemm")
+    check(_L().hx_gemm(_p(a), _p(w), _p(out), M, N, K, a.stride(0), w.stride(0), out.stride(0),
+                       epilogue, _p(residual), residual.stride(0) if residual is not None else 0,
+                       _p(ws), nbytes, code, _stream()), "hx_gemm")
     _count(2 if nbytes else 1)
     return out
 
 
 def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, cos, sin,
-                    cache, q_out=None, batch_offset=0, prefetch=None):
+                    cache, q_out=None, batch_offset=0):
     """Wqkv GEMM with rotary + KV-cache write fused into its epilogue (f16/bf16): returns q
     [rows, n_heads, head_dim]; k, v land in cache[batch_offset + b, pos_start[b] + s]."""
     _require_cuda(x, w_qkv, cache, pos_start)
@@ -171,12 +159,11 @@ def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, 
     code = _code(x)
     nbytes = _L().hx_gemm_workspace(M, N, K, _lib.HX_EPI_QKV_ROTARY, code)
     ws = workspace(nbytes, kind="gemm")
-    pf, pf_bytes = _prefetch_args(prefetch)
-    check(_L().hx_gemm_qkv_rotary_ex(_p(x), _p(w_qkv), M, K, x.stride(0), seqlen, n_heads,
-                                     n_heads_kv, head_dim, _p(pos_start), _p(cos), _p(sin),
-                                     cos.shape[0], _p(q_out), _p(cache), cache.stride(0),
-                                     cache.stride(1), batch_offset, cache.shape[1], _p(ws), nbytes,
-                                     code, pf, pf_bytes, _stream()), "hx_gemm_qkv_rotary")
+    check(_L().hx_gemm_qkv_rotary(_p(x), _p(w_qkv), M, K, x.stride(0), seqlen, n_heads,
+                                  n_heads_kv, head_dim, _p(pos_start), _p(cos), _p(sin),
+                                  cos.shape[0], _p(q_out), _p(cache), cache.stride(0),
+                                  cache.stride(1), batch_offset, cache.shape[1], _p(ws), nbytes,
+                                  code, _stream()), "hx_gemm_qkv_rotary")
     _count(2 if (nbytes and M > 64) else 1)
     return q_out
 

@@ -118,17 +118,6 @@ int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t
  * problems, m <= 64, reduce their K splits inside a thread-block cluster and never need one).
  * Calls that run concurrently need separate workspaces. */
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
-/* hx_gemm with an L2 prefetch hint for the projection that follows on the stream: when the
- * call is decode-shaped (m <= 64), every CTA, once it has issued its last weight load, pulls an
- * equal slice of [l2_prefetch, l2_prefetch + l2_prefetch_bytes) into L2 with bulk prefetches
- * (bytes rounded down to a multiple of 16; l2_prefetch 16-byte aligned, inside one allocation).
- * Nothing is written; the next kernel's first weight loads then hit L2 while HBM keeps
- * streaming across the kernel boundary. Ignored for other shapes. Same call site as hx_gemm
- * (the reference streams every projection's weights cold: mha.py:542, :572, mlp.py:79-87). */
-int hx_gemm_ex(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
-               int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
-               int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
-               const void* l2_prefetch, size_t l2_prefetch_bytes, void* stream);
 /* Which kernel hx_gemm plans for a shape (host-only query, no GPU work): 0 CUDA-core f32,
  * 1 single-SM tcgen05 tiles (128 x 64..256, K split when the tiles are too few), 2 CTA-pair
  * tcgen05 tiles (256 x 256 over two SMs, cta_group::2), 3 decode-shaped (m <= 64: operands
@@ -148,15 +137,6 @@ int hx_gemm_qkv_rotary(const void* x, const void* w_qkv, int64_t m, int64_t k, i
                        int64_t cache_seq_stride, int64_t cache_batch_offset,
                        int64_t cache_max_seq, void* workspace, size_t workspace_bytes, int dtype,
                        void* stream);
-/* hx_gemm_qkv_rotary with hx_gemm_ex's L2 prefetch hint for the next projection. */
-int hx_gemm_qkv_rotary_ex(const void* x, const void* w_qkv, int64_t m, int64_t k, int64_t ldx,
-                       int64_t seqlen, int64_t n_heads, int64_t n_heads_kv, int64_t head_dim,
-                       const int32_t* pos_start, const void* cos_table, const void* sin_table,
-                       int64_t table_rows, void* q_out, void* cache, int64_t cache_batch_stride,
-                       int64_t cache_seq_stride, int64_t cache_batch_offset,
-                       int64_t cache_max_seq, void* workspace, size_t workspace_bytes, int dtype,
-                       const void* l2_prefetch, size_t l2_prefetch_bytes,
-                          void* stream);
 
 /* ---------------------------------------------------------------- attention */
 /* Multi-query (prefill) attention over the KV cache written by hx_rotary_cache_write.
