@@ -739,6 +739,9 @@ def main():
                          "(default: about one prefill GPU per three decode GPUs, TP1)")
     ap.add_argument("--ring-gb", type=float, default=0.0,
                     help="N>1: staging ring per decode rank in GiB (default: sized from the workload)")
+    ap.add_argument("--kv-heads", type=int, default=0,
+                    help="kv_handoff: KV heads per cache (default 8, the full 70B cache; 2 = one "
+                         "TP4 shard)")
     ap.add_argument("--kv-bidir", action="store_true",
                     help="kv_handoff: every GPU sends to (r + N/2) mod N and receives at once")
     ap.add_argument("--requests", type=int, default=64,

@@ -386,7 +386,7 @@ def run_kv_bench(args, bench) -> dict | None:
     bidir = world > 1 and args.kv_bidir
     pairs = [(r, (r + P) % world) for r in range(world if bidir else P)] if world > 1 else []
     sender = world == 1 or any(s == rank for s, _ in pairs)
-    g = KV70B
+    g = dict(KV70B, kv_heads=args.kv_heads or KV70B["kv_heads"])
     row = 2 * g["kv_heads"] * g["head_dim"] * 2
     results = []
     for B in [int(x) for x in args.kv_batches.split(",")]:

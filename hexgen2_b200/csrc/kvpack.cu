@@ -20,17 +20,21 @@ struct PackGeom {
 };
 
 // Maps flat vector index v of request r to (outer, row, chunk) and returns the byte offset
-// inside the capacity-sized cache.
-HX_DEVICE int64_t cache_offset(uint64_t v, uint64_t live, const PackGeom& g) {
-  const uint64_t per_outer = live * (uint64_t)g.row_vecs;
-  const uint64_t outer = v / per_outer;
-  const uint64_t rem = v - outer * per_outer;
-  const uint64_t row = rem / (uint64_t)g.row_vecs;
-  const uint64_t c = rem - row * (uint64_t)g.row_vecs;
+// inside the capacity-sized cache. Idx is 32-bit when every request's vector count fits (the
+// usual case: 80 layers x 4096 rows x 256 vectors < 2^32), which keeps the two divisions
+// per vector cheap.
+template <typename Idx>
+HX_DEVICE int64_t cache_offset(Idx v, Idx live, const PackGeom& g) {
+  const Idx row_vecs = (Idx)g.row_vecs;
+  const Idx per_outer = live * row_vecs;
+  const Idx outer = v / per_outer;
+  const Idx rem = v - outer * per_outer;
+  const Idx row = rem / row_vecs;
+  const Idx c = rem - row * row_vecs;
   return (int64_t)outer * g.outer_stride + (int64_t)row * g.row_stride + (int64_t)c * 16;
 }
 
-template <bool kPack>
+template <bool kPack, typename Idx>
 __global__ void __launch_bounds__(kPackThreads) kv_pack_kernel(
     const uint64_t* __restrict__ cache_ptrs, const int64_t* __restrict__ live_rows,
     const int64_t* __restrict__ packed_offsets, uint8_t* packed, PackGeom g) {
@@ -48,7 +52,7 @@ __global__ void __launch_bounds__(kPackThreads) kv_pack_kernel(
       const uint64_t v = base + (uint64_t)u * kPackThreads;
       if (v < total) {
         if (kPack)
-          buf[u] = __ldg(reinterpret_cast<const uint4*>(cache + cache_offset(v, live, g)));
+          buf[u] = __ldg(reinterpret_cast<const uint4*>(cache + cache_offset<Idx>((Idx)v, (Idx)live, g)));
         else
           buf[u] = __ldg(reinterpret_cast<const uint4*>(pk + v * 16));
       }
@@ -60,7 +64,7 @@ __global__ void __launch_bounds__(kPackThreads) kv_pack_kernel(
         if (kPack)
           *reinterpret_cast<uint4*>(pk + v * 16) = buf[u];
         else
-          *reinterpret_cast<uint4*>(cache + cache_offset(v, live, g)) = buf[u];
+          *reinterpret_cast<uint4*>(cache + cache_offset<Idx>((Idx)v, (Idx)live, g)) = buf[u];
       }
     }
   }
@@ -88,12 +92,20 @@ int launch(bool pack, const uint64_t* cache_ptrs, const int64_t* live_rows,
   int64_t cap = std::max<int64_t>(1, (int64_t)sms * 8 / n_req);
   int gx = (int)std::min<int64_t>(std::max<int64_t>(want, 1), std::max<int64_t>(cap, 1));
   dim3 grid(gx, (unsigned)n_req);
-  if (pack)
-    kv_pack_kernel<true><<<grid, kPackThreads, 0, stream>>>(cache_ptrs, live_rows,
-                                                            packed_offsets, (uint8_t*)packed, g);
+  // 32-bit index math when no request can hold 2^32 vectors (plus the grid stride's headroom).
+  const bool small = max_vecs + (int64_t)gx * kPackThreads * kUnroll < (int64_t(1) << 32);
+  if (pack && small)
+    kv_pack_kernel<true, uint32_t><<<grid, kPackThreads, 0, stream>>>(
+        cache_ptrs, live_rows, packed_offsets, (uint8_t*)packed, g);
+  else if (pack)
+    kv_pack_kernel<true, uint64_t><<<grid, kPackThreads, 0, stream>>>(
+        cache_ptrs, live_rows, packed_offsets, (uint8_t*)packed, g);
+  else if (small)
+    kv_pack_kernel<false, uint32_t><<<grid, kPackThreads, 0, stream>>>(
+        cache_ptrs, live_rows, packed_offsets, (uint8_t*)packed, g);
   else
-    kv_pack_kernel<false><<<grid, kPackThreads, 0, stream>>>(cache_ptrs, live_rows,
-                                                             packed_offsets, (uint8_t*)packed, g);
+    kv_pack_kernel<false, uint64_t><<<grid, kPackThreads, 0, stream>>>(
+        cache_ptrs, live_rows, packed_offsets, (uint8_t*)packed, g);
   HX_LAUNCH_CHECK("kv_pack_kernel");
   return HX_OK;
 }

@@ -239,12 +239,13 @@ class PrefillWorker:
                 [r.prompt], dtype=torch.long).pin_memory().to(dev, non_blocking=True)
             st = CacheState(self.cap, key_value_memory_dict=self.cache)
             tok = m.next_tokens(ids.view(1, L), inference_params=st)
+            live = torch.tensor([L], dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            offs = torch.tensor([off], dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            ops.kv_pack(self.src, torch.tensor([L], dtype=torch.int64, device=dev),
-                        torch.tensor([off], dtype=torch.int64, device=dev), n, self.layer_stride,
-                        self.row_stride, eng.row_bytes, L, self.remotes[r.group])
+            ops.kv_pack(self.src, live, offs, n, self.layer_stride, self.row_stride, eng.row_bytes,
+                        L, self.remotes[r.group])
             e1.record()
             # The pack has completed (its peer stores have landed) before the key is published.
             torch.cuda.current_stream().synchronize()
