@@ -153,6 +153,10 @@ def _serve_tp2(rank, world, port, errors):
     _serve_worker(rank, world, port, errors, (2, 2))
 
 
+def _serve_tp4(rank, world, port, errors):
+    _serve_worker(rank, world, port, errors, (4, 4))
+
+
 def _reshard_two_devices(rank, world, port, errors):
     """Mismatched-TP re-shard with the shards on two GPUs of ONE process: packs run on the
     source's device, unpacks on the destination's (rank 0 does it all; rank 1 does nothing)."""
@@ -230,6 +234,14 @@ def test_streaming_serving_tp2_to_tp2():
     the decode group's collectives in step; greedy tokens via one all-reduce of keys."""
     _need(4)
     _run(_serve_tp2, 4)
+
+
+def test_streaming_serving_tp4_to_tp4():
+    """Prefill TP4 on GPUs 0-3 -> decode TP4 on GPUs 4-7 (BASELINE config 4's split): every
+    TP rank hands its KV-head shard to the decode rank of the same TP index; tokens equal the
+    decode group's own colocated prefill + greedy decode."""
+    _need(8)
+    _run(_serve_tp4, 8)
 
 
 def test_reshard_kv_across_two_devices():
