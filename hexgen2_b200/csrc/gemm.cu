@@ -1332,10 +1332,6 @@ int g_decode_mode = 0;
 
 // Shapes with at least this many 128-row weight tiles run the balanced decode kernel.
 constexpr int kBalMinTiles = 64;
-// The balanced kernel's tile counters sit in a fixed region at the start of the workspace,
-// large enough for this many tiles, so the partials of one shape never overlap the counters
-// of another shape that shares the buffer.
-constexpr int kBalMaxTiles = 4096;
 
 // Balanced-kernel work split and workspace layout for a decode shape.
 struct BalPlan {
@@ -1352,7 +1348,7 @@ BalPlan plan_bal(int m_tiles, int k_blocks, int bn, int sms) {
   for (int t = 0; t < m_tiles; ++t)
     b.max_parts = std::max(b.max_parts,
                            sp.owner((int64_t)(t + 1) * k_blocks - 1) - sp.owner((int64_t)t * k_blocks) + 1);
-  b.ctr_bytes = (size_t)kBalMaxTiles * sizeof(unsigned);
+  b.ctr_bytes = ((size_t)m_tiles * sizeof(unsigned) + 255) / 256 * 256;
   b.bytes = b.ctr_bytes + (size_t)m_tiles * b.max_parts * bn * BM * sizeof(float);
   return b;
 }
@@ -1386,8 +1382,7 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
     p.bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     p.m_tiles = ceil_div(N, BM);
     p.n_tiles = 1;
-    p.bal = p.m_tiles <= kBalMaxTiles &&
-            (g_decode_mode == 2 || (g_decode_mode == 0 && p.m_tiles >= kBalMinTiles));
+    p.bal = g_decode_mode == 2 || (g_decode_mode == 0 && p.m_tiles >= kBalMinTiles);
   } else {
     p.m_tiles = ceil_div(M, BM);
     const int64_t t256 = (int64_t)p.m_tiles * ceil_div(N, 256);

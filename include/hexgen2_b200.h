@@ -115,9 +115,8 @@ int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t
             void* stream);
 /* Workspace bytes for hx_gemm / hx_gemm_qkv_rotary (0 = none needed):
  *  - m > 64 and too few output tiles to fill the GPU: f32 split-K partial sums;
- *  - decode-shaped (m <= 64) with 64..4096 weight tiles of 128 rows (8065 <= n <= 524288):
- *    the balanced decode kernel's tile counters (a fixed 16 KB region at the start) + f32
- *    partials. Its workspace must be ZERO-FILLED before
+ *  - decode-shaped (m <= 64) with >= 64 weight tiles of 128 rows (n >= 8065): the balanced
+ *    decode kernel's tile counters + f32 partials. Its workspace must be ZERO-FILLED before
  *    the first call (256-byte aligned); every call leaves the counters at zero again, so one
  *    zeroed buffer serves any number of calls. After a call that reported a device error
  *    (hx_device_error), zero it again.
