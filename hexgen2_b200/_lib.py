@@ -35,7 +35,6 @@ _SIGNATURES = {
                         c_void_p]),
     "hx_gemm_workspace": (c_size_t, [c_int64, c_int64, c_int64, c_int, c_int]),
     "hx_gemm_kernel_kind": (c_int, [c_int64, c_int64, c_int64, c_int]),
-    "hx_gemm_set_decode_mode": (c_int, [c_int]),
     "hx_gemm_qkv_rotary": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                                    c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
                                    c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,

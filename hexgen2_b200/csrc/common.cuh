@@ -20,7 +20,6 @@
 #include "../../include/hexgen2_b200.h"
 
 #define HX_DEVICE __device__ __forceinline__
-#define HX_DEVICE_HOST __host__ __device__ __forceinline__
 
 // ---------------------------------------------------------------------------------------
 // Host-side error reporting (thread-local message, returned through hx_last_error()).

@@ -727,251 +727,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
 }
 
-// ------------------------------------------------------------------------------------------
-// Balanced decode-shaped GEMM (many weight tiles): one CTA per SM, each streaming an equal
-// share of the (tile, k-block) units through a ~200 KB ring.
-//
-// With more 128-row weight tiles than SMs the cluster kernel above runs 1-2 CTAs per SM with
-// ~100 KB rings; too few bytes are in flight per SM to keep HBM busy, and SMs holding two CTAs
-// finish last. Here units u = tile * k_blocks + kb are split evenly over G = min(SMs, units)
-// CTAs (CTA c owns [c*U/G, (c+1)*U/G)), so every SM streams the same number of weight bytes.
-// A CTA's range covers consecutive segments (tile, kb range); the MMA warp accumulates each
-// segment into one of two TMEM accumulators (the epilogue of one segment overlaps the MMAs of
-// the next). A tile owned by one CTA is stored directly. A tile split across CTAs: every part
-// writes its f32 partial [BN][128] to the workspace, then takes a ticket from the tile's
-// counter (atomicAdd after a fence); the CTA drawing the last ticket sums ALL parts in part
-// order (so the result does not depend on arrival order), applies the epilogue and resets the
-// counter to 0 for the next launch. No CTA ever waits for another.
-// Workspace: [tile counters, zero-initialised once by the caller][partials].
-// ------------------------------------------------------------------------------------------
-struct BalSplit {
-  int64_t units;  // m_tiles * k_blocks
-  int grid;
-  HX_DEVICE_HOST int64_t lo(int c) const { return (int64_t)c * units / grid; }
-  HX_DEVICE_HOST int owner(int64_t u) const {
-    int c = (int)((u * grid) / units);
-    while (c + 1 < grid && lo(c + 1) <= u) ++c;
-    while (c > 0 && lo(c) > u) --c;
-    return c;
-  }
-};
-
-template <typename T, int BN, int EPI>
-HX_DEVICE void bal_store_rows(const GemmArgs& a, int n, int lane, const int* pos_s,
-                              const float (&v)[BN]) {
-  const int rows = min(BN, a.M);
-#pragma unroll
-  for (int b0 = 0; b0 < BN; b0 += 8) {
-    if (b0 < rows) {
-      int bs[8];
-      float vals[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        bs[i] = b0 + i;
-        vals[i] = v[b0 + i];
-      }
-      const int nr = min(8, rows - b0);
-      Epi8<T, EPI> e;
-      sk_load8<T, EPI>(a, bs, nr, n, lane, pos_s, e);
-      sk_store8<T, EPI>(a, bs, nr, n, lane, vals, e);
-    }
-  }
-}
-
-template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_decode_bal_kernel(const __grid_constant__ CUtensorMap tmW,
-                           const __grid_constant__ CUtensorMap tmX, const GemmArgs a, int stages,
-                           int max_parts, unsigned* __restrict__ tile_ctr,
-                           float* __restrict__ partials) {
-  constexpr int kWBytes = BM * BK * 2;
-  constexpr int kXBytes = BN * BK * 2;
-  constexpr int kStageBytes = kWBytes + kXBytes;
-  constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
-  constexpr uint32_t kTmemCols = 2 * kAccCols;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * kStageBytes);
-  uint64_t* empty = full + kDecMaxStages;
-  uint64_t* tfull = empty + kDecMaxStages;  // [2]
-  uint64_t* tempty = tfull + 2;             // [2]
-  uint32_t* counters = reinterpret_cast<uint32_t*>(tempty + 2);  // [0] loads issued, [1] consumed
-  uint32_t* tmem_slot = counters + 2;
-  int* last_flag = reinterpret_cast<int*>(counters + 3);
-  int* pos_s = reinterpret_cast<int*>(counters + 4);  // [BN] row positions (Wqkv)
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KB = a.k_blocks;
-  const BalSplit sp{(int64_t)a.m_tiles * KB, (int)gridDim.x};
-  const int64_t u0 = sp.lo(blockIdx.x), u1 = sp.lo(blockIdx.x + 1);
-
-  if (threadIdx.x == 0) {
-    prefetch_tensormap(&tmW);
-    prefetch_tensormap(&tmX);
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
-    }
-    counters[0] = counters[1] = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  if (!(warp == 0 && lane == 0)) pdl_wait();  // the producer waits after its weight prefetch
-  pdl_trigger();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // Weights do not depend on earlier kernels: the first ring of weight tiles is requested
-      // before waiting for the previous kernel; activation tiles after.
-      const int npre = (int)(u1 - u0 < (int64_t)stages ? u1 - u0 : (int64_t)stages);
-      for (int i = 0; i < npre; ++i) {
-        const int64_t u = u0 + i;
-        mbar_arrive_expect_tx(&full[i], kStageBytes);
-        tma_load_2d(ring + i * kStageBytes, &tmW, &full[i], (int)(u % KB) * BK, (int)(u / KB) * BM);
-      }
-      pdl_wait();
-      for (int i = 0; i < npre; ++i)
-        tma_load_2d(ring + i * kStageBytes + kWBytes, &tmX, &full[i], (int)((u0 + i) % KB) * BK, 0);
-      int stage = npre == stages ? 0 : npre;
-      uint32_t phase = npre == stages ? 1 : 0, issued = npre;
-      for (int64_t u = u0 + npre; u < u1; ++u) {
-        if (!mbar_wait(&empty[stage], phase ^ 1)) break;
-        mbar_arrive_expect_tx(&full[stage], kStageBytes);
-        uint8_t* st = ring + stage * kStageBytes;
-        tma_load_2d(st, &tmW, &full[stage], (int)(u % KB) * BK, (int)(u / KB) * BM);
-        tma_load_2d(st + kWBytes, &tmX, &full[stage], (int)(u % KB) * BK, 0);
-        ++issued;
-        if (++stage == stages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      counters[0] = issued;
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16<T>(BM, BN);
-      int stage = 0, seg = 0;
-      uint32_t phase = 0, consumed = 0;
-      bool ok = true;
-      for (int64_t u = u0; u < u1 && ok; ++seg) {
-        const int64_t t = u / KB;
-        const int64_t seg_lo = u, seg_hi = (t + 1) * KB < u1 ? (t + 1) * KB : u1;
-        const int buf = seg & 1;
-        if (!mbar_wait(&tempty[buf], ((seg >> 1) & 1) ^ 1)) break;
-        tc_fence_after();
-        const uint32_t acc = tmem_base + buf * kAccCols;
-        for (; u < seg_hi; ++u) {
-          if (!mbar_wait(&full[stage], phase)) {
-            ok = false;
-            break;
-          }
-          ++consumed;
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(ring + stage * kStageBytes);
-          const uint32_t b_addr = a_addr + kWBytes;
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            tc_mma_f16(acc, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
-                       idesc, (u > seg_lo || k > 0) ? 1u : 0u);
-          tc_commit(&empty[stage]);
-          if (++stage == stages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        // Completes once the segment's MMAs have finished (after a timed-out wait the
-        // accumulator is incomplete; the device error word already says so).
-        tc_commit(&tfull[buf]);
-      }
-      counters[1] = consumed;
-    }
-  } else {
-    // Epilogue warps 2..5: TMEM lane quarter = warp % 4 = weight rows 32q..32q+31 of a tile.
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    if (EPI == HX_EPI_QKV_ROTARY) {
-      const QkvArgs& q = a.qkv;
-      for (int m = threadIdx.x - 64; m < min(BN, a.M); m += 128)
-        pos_s[m] = q.pos_start[m / q.seqlen] + m % q.seqlen;
-      named_bar_sync(2, 128);
-    }
-    int seg = 0;
-    for (int64_t u = u0; u < u1; ++seg) {
-      const int64_t t = u / KB;
-      const int64_t seg_hi = (t + 1) * KB < u1 ? (t + 1) * KB : u1;
-      const int buf = seg & 1;
-      const bool ready = mbar_wait_warp(&tfull[buf], (seg >> 1) & 1);
-      tc_fence_after();
-      float v[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 16; ++c) {
-        uint32_t x[16];
-        if (ready) {
-          tmem_ld_32x32b_x16(tmem_base + buf * kAccCols + ((uint32_t)(quarter * 32) << 16) + c * 16, x);
-          tc_wait_ld();
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[c * 16 + j] = ready ? __uint_as_float(x[j]) : 0.f;
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty[buf]);
-      const int first = sp.owner(t * KB), last = sp.owner((t + 1) * KB - 1);
-      const int parts = last - first + 1;
-      const int n = (int)t * BM + r;
-      if (parts == 1) {
-        bal_store_rows<T, BN, EPI>(a, n, lane, pos_s, v);
-      } else {
-        const int p = (int)blockIdx.x - first;
-        float* mine = partials + ((int64_t)t * max_parts + p) * (BN * BM);
-#pragma unroll
-        for (int b = 0; b < BN; ++b) mine[b * BM + r] = v[b];
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 64) *last_flag = atomicAdd(&tile_ctr[t], 1u) == (unsigned)(parts - 1);
-        named_bar_sync(1, 128);
-        if (*last_flag) {
-          __threadfence();
-          float sum[BN];
-#pragma unroll
-          for (int b = 0; b < BN; ++b) sum[b] = 0.f;
-          for (int q = 0; q < parts; ++q) {
-            const float* src = partials + ((int64_t)t * max_parts + q) * (BN * BM);
-#pragma unroll
-            for (int b = 0; b < BN; ++b) sum[b] += __ldcg(src + b * BM + r);
-          }
-          bal_store_rows<T, BN, EPI>(a, n, lane, pos_s, sum);
-          if (threadIdx.x == 64) tile_ctr[t] = 0u;  // ready for the next launch
-        }
-      }
-      u = seg_hi;
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  // After an aborted wait, loads may have been issued that nobody consumed: let them land
-  // (bounded) before the CTA's shared memory goes away.
-  if (threadIdx.x == 0) {
-    for (uint32_t i = counters[1]; i < counters[0]; ++i)
-      if (!mbar_wait_drain(&full[i % stages], (i / stages) & 1)) break;
-  }
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
-}
-
 // Split-K reduction in split order + epilogue. One thread per output element.
 template <typename T, int EPI>
 __global__ void splitk_reduce_kernel(const GemmArgs a) {
@@ -1323,35 +1078,7 @@ struct Plan {
   int bn, m_tiles, n_tiles, k_splits, kb_per_split, k_blocks;
   bool swap;    // decode-shaped: operands swapped, split-K inside a cluster (chosen at launch)
   bool pair;    // 256 x 256 tiles on CTA pairs (gemm_pair_kernel)
-  bool bal;     // decode-shaped on the balanced kernel (gemm_decode_bal_kernel)
 };
-
-// Decode-shaped kernel choice: 0 = by shape, 1 = always the cluster kernel, 2 = always the
-// balanced kernel (hx_gemm_set_decode_mode; diagnostics and tests).
-int g_decode_mode = 0;
-
-// Shapes with at least this many 128-row weight tiles run the balanced decode kernel.
-constexpr int kBalMinTiles = 64;
-
-// Balanced-kernel work split and workspace layout for a decode shape.
-struct BalPlan {
-  int grid, max_parts;
-  size_t ctr_bytes, bytes;
-};
-
-BalPlan plan_bal(int m_tiles, int k_blocks, int bn, int sms) {
-  BalPlan b;
-  const int64_t units = (int64_t)m_tiles * k_blocks;
-  b.grid = (int)std::min<int64_t>(sms, units);
-  const BalSplit sp{units, b.grid};
-  b.max_parts = 1;
-  for (int t = 0; t < m_tiles; ++t)
-    b.max_parts = std::max(b.max_parts,
-                           sp.owner((int64_t)(t + 1) * k_blocks - 1) - sp.owner((int64_t)t * k_blocks) + 1);
-  b.ctr_bytes = ((size_t)m_tiles * sizeof(unsigned) + 255) / 256 * 256;
-  b.bytes = b.ctr_bytes + (size_t)m_tiles * b.max_parts * bn * BM * sizeof(float);
-  return b;
-}
 
 // Work items of the CTA-pair kernel: (256-row block, 256-column block).
 int64_t pair_items(int64_t M, int64_t N) { return (int64_t)ceil_div(M, 2 * BM) * ceil_div(N, 256); }
@@ -1366,7 +1093,6 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
   Plan p;
   p.k_blocks = ceil_div(K, BK);
   p.swap = M <= 64;
-  p.bal = false;
   // CTA pairs when there are rows for both halves and at least ~3/7 of the pairs get an item:
   // a pair moves half the shared-memory bytes per FLOP of a single-SM tile, so even a partly
   // filled wave of pairs beats two waves of shared-memory-bound single-SM tiles (measured at
@@ -1382,7 +1108,6 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
     p.bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     p.m_tiles = ceil_div(N, BM);
     p.n_tiles = 1;
-    p.bal = g_decode_mode == 2 || (g_decode_mode == 0 && p.m_tiles >= kBalMinTiles);
   } else {
     p.m_tiles = ceil_div(M, BM);
     const int64_t t256 = (int64_t)p.m_tiles * ceil_div(N, 256);
@@ -1403,7 +1128,6 @@ Plan plan_gemm(int64_t M, int64_t N, int64_t K) {
 }
 
 size_t plan_workspace(const Plan& p, int64_t M, int64_t N) {
-  if (p.swap && p.bal) return plan_bal(p.m_tiles, p.k_blocks, p.bn, device_sms()).bytes;
   if (p.swap || p.pair) return 0;
   return p.k_splits > 1 ? (size_t)p.k_splits * M * N * sizeof(float) : 0;
 }
@@ -1449,39 +1173,6 @@ int launch_decode(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& 
                           "gemm_decode_kernel launch");
   if (s) return s;
   HX_LAUNCH_CHECK("gemm_decode_kernel");
-  return HX_OK;
-}
-
-// Balanced decode launch: one CTA per SM (or per unit when there are fewer), ~200 KB ring.
-template <typename T, int BN, int EPI>
-int launch_decode_bal(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& a,
-                      void* ws, size_t ws_bytes, cudaStream_t stream) {
-  auto kern = gemm_decode_bal_kernel<T, BN, EPI>;
-  constexpr int stage_bytes = BM * BK * 2 + BN * BK * 2;
-  constexpr size_t smem_fixed = 1024 + 2 * kDecMaxStages * 8 + 4 * 8 + 16 + 64 * sizeof(int);
-  const int stages = std::max(2, std::min(kDecMaxStages, 200 * 1024 / stage_bytes));
-  const size_t smem = smem_fixed + (size_t)stages * stage_bytes;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    int s = hx::cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem),
-                            "cudaFuncSetAttribute(gemm_decode_bal)");
-    if (s) return s;
-    attr_set[dev & 63] = true;
-  }
-  const BalPlan b = plan_bal(a.m_tiles, a.k_blocks, BN, device_sms());
-  HX_REQUIRE(ws && ws_bytes >= b.bytes, "hx_gemm: decode workspace too small (%zu < %zu)", ws_bytes,
-             b.bytes);
-  HX_REQUIRE((uintptr_t)ws % 256 == 0, "hx_gemm: workspace must be 256-byte aligned");
-  unsigned* ctr = static_cast<unsigned*>(ws);
-  float* parts = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + b.ctr_bytes);
-  int s = hx::cuda_status(launch_ex(kern, dim3((unsigned)b.grid), dim3(kGemmThreads), smem, stream,
-                                    1, mw, mx, a, stages, b.max_parts, ctr, parts),
-                          "gemm_decode_bal_kernel launch");
-  if (s) return s;
-  HX_LAUNCH_CHECK("gemm_decode_bal_kernel");
   return HX_OK;
 }
 
@@ -1552,7 +1243,7 @@ int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int6
   a.ws = nullptr;
   if (qkv) a.qkv = *qkv;
   const size_t need = plan_workspace(p, M, N);
-  if (need && !p.swap) {
+  if (need) {
     HX_REQUIRE(ws && ws_bytes >= need, "hx_gemm: workspace too small (%zu < %zu)", ws_bytes, need);
     HX_REQUIRE((uintptr_t)ws % 16 == 0, "hx_gemm: workspace must be 16-byte aligned");
     a.ws = (float*)ws;
@@ -1573,13 +1264,6 @@ int gemm_half(const void* A, const void* B, void* Cp, int64_t M, int64_t N, int6
     if (s) return s;
     s = make_map(&mb, A, M, K, lda, p.bn, dtype);
     if (s) return s;
-    if (p.bal) {
-      switch (p.bn) {
-        case 16: return launch_decode_bal<T, 16, EPI>(ma, mb, a, ws, ws_bytes, stream);
-        case 32: return launch_decode_bal<T, 32, EPI>(ma, mb, a, ws, ws_bytes, stream);
-        default: return launch_decode_bal<T, 64, EPI>(ma, mb, a, ws, ws_bytes, stream);
-      }
-    }
     switch (p.bn) {
       case 16: return launch_decode<T, 16, EPI>(ma, mb, a, stream);
       case 32: return launch_decode<T, 32, EPI>(ma, mb, a, stream);
@@ -1655,14 +1339,7 @@ int hx_gemm_kernel_kind(int64_t m, int64_t n, int64_t k, int dtype) {
   if (m <= 0 || n <= 0 || k <= 0) return -1;
   if (dtype == HX_F32) return 0;
   const Plan p = plan_gemm(m, n, k);
-  return p.swap ? (p.bal ? 4 : 3) : (p.pair ? 2 : 1);
-}
-
-int hx_gemm_set_decode_mode(int mode) {
-  HX_REQUIRE(mode >= 0 && mode <= 2, "hx_gemm_set_decode_mode: mode must be 0, 1 or 2");
-  const int old = g_decode_mode;
-  g_decode_mode = mode;
-  return old;
+  return p.swap ? 3 : (p.pair ? 2 : 1);
 }
 
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype) {

@@ -56,9 +56,7 @@ def _count(launches=1):
 
 def workspace(nbytes: int, device=None, kind: str = "attn") -> torch.Tensor | None:
     """Per-device scratch buffer of at least nbytes (None for 0), one per kind, reused across
-    calls on the same stream (GEMM split-K partials, decode-attention split partials, and the
-    balanced decode GEMM's tile counters + partials: kind "gemm_dec", zero-filled when allocated
-    because its counters must start at zero; every call leaves them at zero)."""
+    calls on the same stream (GEMM split-K partials, decode-attention split partials)."""
     if nbytes == 0:
         return None
     dev = torch.cuda.current_device() if device is None else torch.device(device).index
@@ -67,8 +65,7 @@ def workspace(nbytes: int, device=None, kind: str = "attn") -> torch.Tensor | No
     if buf is None or buf.numel() < nbytes:
         global WORKSPACE_GEN
         size = max(nbytes, 0 if buf is None else buf.numel() * 2)
-        alloc = torch.zeros if kind == "gemm_dec" else torch.empty
-        buf = alloc(size, dtype=torch.uint8, device=f"cuda:{dev}")
+        buf = torch.empty(size, dtype=torch.uint8, device=f"cuda:{dev}")
         _workspaces[key] = buf
         WORKSPACE_GEN += 1
     return buf
@@ -142,11 +139,11 @@ def gemm(a, w, epilogue=HX_EPI_NONE, residual=None, out=None):
         out = torch.empty(M, n_out, dtype=a.dtype, device=a.device)
     code = _code(a)
     nbytes = _L().hx_gemm_workspace(M, N, K, epilogue, code)
-    ws = workspace(nbytes, kind=("gemm_dec" if M <= 64 else "gemm") if code != _lib.HX_F32 else "attn")
+    ws = workspace(nbytes, kind="gemm" if code != _lib.HX_F32 else "attn")
     check(_L().hx_gemm(_p(a), _p(w), _p(out), M, N, K, a.stride(0), w.stride(0), out.stride(0),
                        epilogue, _p(residual), residual.stride(0) if residual is not None else 0,
                        _p(ws), nbytes, code, _stream()), "hx_gemm")
-    _count(2 if (nbytes and M > 64) else 1)
+    _count(2 if nbytes else 1)
     return out
 
 
@@ -161,7 +158,7 @@ def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, 
         q_out = torch.empty(M, n_heads, head_dim, dtype=x.dtype, device=x.device)
     code = _code(x)
     nbytes = _L().hx_gemm_workspace(M, N, K, _lib.HX_EPI_QKV_ROTARY, code)
-    ws = workspace(nbytes, kind="gemm_dec" if M <= 64 else "gemm")
+    ws = workspace(nbytes, kind="gemm")
     check(_L().hx_gemm_qkv_rotary(_p(x), _p(w_qkv), M, K, x.stride(0), seqlen, n_heads,
                                   n_heads_kv, head_dim, _p(pos_start), _p(cos), _p(sin),
                                   cos.shape[0], _p(q_out), _p(cache), cache.stride(0),
@@ -169,14 +166,6 @@ def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, 
                                   code, _stream()), "hx_gemm_qkv_rotary")
     _count(2 if (nbytes and M > 64) else 1)
     return q_out
-
-
-def set_decode_gemm_mode(mode: int) -> int:
-    """0 = choose the decode GEMM kernel by shape, 1 = cluster split-K kernel, 2 = balanced
-    kernel (diagnostics and tests). Returns the previous mode. Scratch sizes depend on it."""
-    global WORKSPACE_GEN
-    WORKSPACE_GEN += 1  # kept CUDA graphs captured the other kernel
-    return _L().hx_gemm_set_decode_mode(int(mode))
 
 
 def gemm_workspace_bytes(M, N, K, epilogue, dtype) -> int:

@@ -113,27 +113,15 @@ int hx_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t
             int64_t lda, int64_t ldb, int64_t ldc, int epilogue, const void* residual,
             int64_t ld_residual, void* workspace, size_t workspace_bytes, int dtype,
             void* stream);
-/* Workspace bytes for hx_gemm / hx_gemm_qkv_rotary (0 = none needed):
- *  - m > 64 and too few output tiles to fill the GPU: f32 split-K partial sums;
- *  - decode-shaped (m <= 64) with >= 64 weight tiles of 128 rows (n >= 8065): the balanced
- *    decode kernel's tile counters + f32 partials. Its workspace must be ZERO-FILLED before
- *    the first call (256-byte aligned); every call leaves the counters at zero again, so one
- *    zeroed buffer serves any number of calls. After a call that reported a device error
- *    (hx_device_error), zero it again.
- * Smaller decode shapes reduce their K splits inside a thread-block cluster and need none.
+/* Workspace bytes for hx_gemm / hx_gemm_qkv_rotary: f32 split-K partial sums, needed only
+ * when m > 64 and the output has too few tiles to fill the GPU (0 otherwise; decode-shaped
+ * problems, m <= 64, reduce their K splits inside a thread-block cluster and never need one).
  * Calls that run concurrently need separate workspaces. */
 size_t hx_gemm_workspace(int64_t m, int64_t n, int64_t k, int epilogue, int dtype);
-/* Decode-shaped kernel choice for later hx_gemm / hx_gemm_workspace calls of this process:
- * 0 = by shape (default), 1 = always the cluster split-K kernel, 2 = always the balanced
- * kernel. Returns the previous mode. Diagnostic (kernel comparison and tests); no reference
- * counterpart. */
-int hx_gemm_set_decode_mode(int mode);
 /* Which kernel hx_gemm plans for a shape (host-only query, no GPU work): 0 CUDA-core f32,
  * 1 single-SM tcgen05 tiles (128 x 64..256, K split when the tiles are too few), 2 CTA-pair
  * tcgen05 tiles (256 x 256 over two SMs, cta_group::2), 3 decode-shaped (m <= 64: operands
- * swapped, K split inside a cluster), 4 decode-shaped on the balanced kernel (one CTA per SM,
- * equal k-block ranges, split tiles reduced through the workspace). Diagnostic; no reference
- * counterpart. */
+ * swapped, K split inside a cluster). Diagnostic; no reference counterpart. */
 int hx_gemm_kernel_kind(int64_t m, int64_t n, int64_t k, int dtype);
 
 /* Wqkv projection fused with rotary and the KV-cache write: computes qkv = x * Wqkv^T
