@@ -27,6 +27,13 @@ from .checkpoint import (llama_config_to_gpt2_config, load_safetensors_dir, mode
 from .gpt import CacheState, GPTLMHeadModel
 
 
+# Packed prefill passes: at most this many tokens (GEMM rows) and prompts per pass. 8192 rows
+# fill every CTA pair of the projection GEMMs; the cap on prompts bounds the cache slots a
+# prefill-only rank needs.
+PREFILL_TOKENS = 8192
+PREFILL_PROMPTS = 16
+
+
 def _check_device(device: torch.device):
     if device.type != "cuda" or not torch.cuda.is_available():
         raise ValueError("Native HexGen-2 on B200 requires CUDA; the CPU reference lives in the oracle")
@@ -264,11 +271,35 @@ class Engine:
         self.__dict__.pop("_decode_graphs", None)
 
     @torch.inference_mode()
+    def prefill_chunks(self, ids, lengths, cache, first, events=None,
+                       max_tokens=PREFILL_TOKENS, max_prompts=PREFILL_PROMPTS):
+        """Prefills prompts (flat device ids, prompt b of lengths[b] tokens into batch row b of
+        `cache`) in packed passes of at most max_tokens tokens / max_prompts prompts
+        (GPTLMHeadModel.prefill_packed), writing each greedy first token into first[b]. With
+        events, events[b] is recorded when prompt b's first token is ready."""
+        offs = [0]
+        for L in lengths:
+            offs.append(offs[-1] + L)
+        b0 = 0
+        while b0 < len(lengths):
+            b1, tok = b0, 0
+            while b1 < len(lengths) and b1 - b0 < max_prompts and (
+                    b1 == b0 or tok + lengths[b1] <= max_tokens):
+                tok += lengths[b1]
+                b1 += 1
+            self.model.prefill_packed(ids[offs[b0]:offs[b1]], lengths[b0:b1], cache,
+                                      list(range(b0, b1)), out=first[b0:b1])
+            if events is not None:
+                for b in range(b0, b1):
+                    events[b].record()
+            b0 = b1
+
     def serve_batch(self, prompts, lengths=None, max_new_tokens=16):
         """Colocated greedy generation for a batch of requests: prompts as a list of token-id
-        lists, or a flat (ideally pinned) int64 CPU tensor plus per-request lengths. Each
-        request is prefilled straight into its slot of one all-layer cache, then the whole
-        ragged batch decodes together. Returns a list of max_new_tokens tokens per request."""
+        lists, or a flat (ideally pinned) int64 CPU tensor plus per-request lengths. The
+        prompts are prefilled in packed passes straight into their slots of one all-layer
+        cache, then the whole ragged batch decodes together. Returns a list of max_new_tokens
+        tokens per request."""
         if isinstance(prompts, torch.Tensor):
             flat, lens = prompts, list(lengths)
         else:
@@ -279,14 +310,7 @@ class Engine:
         ids = flat.to(self.device, non_blocking=True)
         cache = self.model.allocate_inference_cache(B, capacity)
         first = torch.empty(B, dtype=torch.long, device=self.device)
-        off = 0
-        for b, L in enumerate(lens):
-            st = CacheState(capacity, max_batch_size=B, batch_size_offset=b,
-                            key_value_memory_dict=cache)
-            logits = self.model(ids[off:off + L].view(1, L), inference_params=st,
-                                last_token_only=True).logits
-            ops.argmax(logits, out=first[b:b + 1])
-            off += L
+        self.prefill_chunks(ids, lens, cache, first)
         lengths_dev = torch.tensor(lens, dtype=torch.int32).to(self.device, non_blocking=True)
         toks = self.decode_batch(first, cache, lengths_dev, max_new_tokens - 1)
         return toks.cpu().tolist()

@@ -401,6 +401,94 @@ class GPTLMHeadModel(nn.Module):
         return CausalLMOutput(logits=logits)
 
     @torch.inference_mode()
+    def prefill_packed(self, input_ids, lengths, caches, slots, greedy=True, out=None):
+        """Prefill of several prompts in ONE pass over their concatenated rows: input_ids is a
+        flat int64 CUDA tensor of sum(lengths) tokens, prompt i of lengths[i] tokens goes to
+        batch row slots[i] of `caches` ({layer: [B, capacity, 2, hkv, d]}, positions 0..L-1).
+        Every projection, norm and residual add runs once over all rows (GEMM M = sum of the
+        prompt lengths, which fills the GPU where a single prompt's rows do not); Wqkv runs as a
+        plain GEMM and each prompt's rotary + cache write and causal attention run on its own
+        row slice. Equals forward() of each prompt alone, logit for logit up to the summation
+        order of the projections. Returns the greedy next token of every prompt (int64 [n]; TP:
+        one all-reduce of keys, as next_tokens) or, with greedy=False, the last-token logits
+        [n, vocab] (gathered across TP ranks)."""
+        n = len(lengths)
+        if n == 0 or len(slots) != n or any(L <= 0 for L in lengths):
+            raise ValueError("prefill_packed needs one slot and a positive length per prompt")
+        T = int(sum(lengths))
+        if input_ids.dim() != 1 or input_ids.numel() != T:
+            raise ValueError("input_ids must be the flat concatenation of the prompts")
+        w_emb = self.transformer.embeddings.word_embeddings.weight
+        device, dtype = w_emb.device, w_emb.dtype
+        h, hq, hk, d = self.hidden, self.hq, self.hk, self.head_dim
+        cap = caches[0].shape[1]
+        if max(lengths) > cap:
+            raise ValueError(f"a prompt of {max(lengths)} tokens exceeds the cache capacity {cap}")
+        cos, sin = self.rope_tables(cap, device, dtype)
+        ids = input_ids.to(device=device, dtype=torch.long)
+        zero = torch.zeros(1, dtype=torch.int32, device=device)
+        offs = [0]
+        for L in lengths:
+            offs.append(offs[-1] + L)
+        residual = torch.empty(T, h, dtype=dtype, device=device)
+        normed = torch.empty(T, h, dtype=dtype, device=device)
+        q = torch.empty(T, hq, d, dtype=dtype, device=device)
+        ctx = torch.empty(T, hq, d, dtype=dtype, device=device)
+        layers = self.transformer.layers
+        if self.tp == 1:
+            ops.embed_rmsnorm(ids, w_emb, layers[0].norm1.weight, self.eps, residual, normed)
+        else:
+            emb = self.transformer.embeddings(ids.view(1, T)).view(T, h)
+            ops.rmsnorm(emb, layers[0].norm1.weight, self.eps, residual_out=residual, out=normed)
+        for i, layer in enumerate(layers):
+            mixer, mlp = layer.mixer, layer.mlp
+            cache = caches[i]
+            qkv = ops.gemm(normed, mixer.Wqkv.weight)
+            for b in range(n):
+                o, L = offs[b], lengths[b]
+                ops.rotary_cache_write(qkv[o:o + L], 1, L, hq, hk, d, zero, cos, sin, cache,
+                                       q_out=q[o:o + L].view(1, L, hq, d), batch_offset=slots[b],
+                                       interleaved=mixer.rotary_emb_interleaved)
+                ops.prefill_attention(q[o:o + L].view(1, L, hq, d), cache, zero, hk, self.scale,
+                                      causal=True, out=ctx[o:o + L].view(1, L, hq, d),
+                                      batch_offset=slots[b])
+            c2 = ctx.view(T, hq * d)
+            if self.tp == 1:
+                ops.gemm(c2, mixer.out_proj.weight, HX_EPI_RESIDUAL, residual=residual, out=residual)
+                ops.rmsnorm(residual, layer.norm2.weight, self.eps, out=normed)
+            else:
+                part = ops.gemm(c2, mixer.out_proj.weight)
+                self._all_reduce(part)
+                ops.rmsnorm(part, layer.norm2.weight, self.eps, add=residual,
+                            residual_out=residual, out=normed)
+            act = ops.gemm(normed, mlp.fc1.weight, HX_EPI_SWIGLU)
+            nxt = layers[i + 1].norm1.weight if i + 1 < len(layers) else None
+            if self.tp == 1:
+                ops.gemm(act, mlp.fc2.weight, HX_EPI_RESIDUAL, residual=residual, out=residual)
+                if nxt is not None:
+                    ops.rmsnorm(residual, nxt, self.eps, out=normed)
+            else:
+                part = ops.gemm(act, mlp.fc2.weight)
+                self._all_reduce(part)
+                ops.rmsnorm(part, nxt if nxt is not None else self.transformer.ln_f.weight,
+                            self.eps, add=residual, residual_out=residual, out=normed)
+        last = torch.tensor([o - 1 for o in offs[1:]], dtype=torch.long, device=device)
+        if self.tp > 1:
+            hfin = normed.index_select(0, last)
+        else:
+            hfin = ops.rmsnorm(residual.index_select(0, last), self.transformer.ln_f.weight, self.eps)
+        logits = ops.gemm(hfin, self.lm_head.weight)
+        if greedy:
+            if self.tp == 1:
+                return ops.argmax(logits, out=out)
+            return self._tp_argmax(logits, out)
+        if self.tp > 1:
+            parts = [torch.empty_like(logits) for _ in range(self.tp)]
+            dist.all_gather(parts, logits, group=self.process_group)
+            logits = torch.cat(parts, dim=-1)
+        return logits
+
+    @torch.inference_mode()
     def next_tokens(self, input_ids, inference_params=None, out=None):
         """Greedy next token of every sequence: argmax of forward(..., last_token_only=True)
         with torch.argmax's tie rule (lowest vocabulary index). Returns int64 [batch].

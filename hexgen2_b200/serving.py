@@ -40,7 +40,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .engine import ContinuousBatcher
+from .engine import PREFILL_PROMPTS, PREFILL_TOKENS, ContinuousBatcher
 from .gpt import CacheState
 from .transport import KVHandoff
 
@@ -192,30 +192,39 @@ def connect_rings(split: Split, ring_bytes: int):
 
 
 class PrefillWorker:
-    """One prefill rank: prefill at batch 1, greedy first token, pack into the decode peer's ring."""
+    """One prefill rank: packed prefill of the requests that have arrived, greedy first tokens,
+    one gather-pack per request into its decode peer's ring."""
 
     def __init__(self, engine, split: Split, store, remotes: dict, ring_bytes: int,
-                 max_prompt: int):
+                 max_prompt: int, max_tokens: int = PREFILL_TOKENS,
+                 max_prompts: int = PREFILL_PROMPTS):
         self.eng, self.split, self.store = engine, split, store
         kind, self.g, self.t = split.role(dist.get_rank())
         assert kind == "prefill"
         self.remotes = remotes
         self.rings = {j: ByteRing(ring_bytes) for j in remotes}
+        self.max_tokens, self.max_prompts = max(max_tokens, max_prompt), max_prompts
         m = engine.model
-        self.cap = max_prompt + 1
-        self.cache = m.allocate_inference_cache(1, self.cap)
+        self.cap = max_prompt
+        self.cache = m.allocate_inference_cache(max_prompts, self.cap)
         c0 = self.cache[0]
         self.elem = c0.element_size()
         self.layer_stride = self.cache[1].data_ptr() - c0.data_ptr() if m.n_layer > 1 else 0
         self.row_stride = c0.stride(1) * self.elem
-        self.src = torch.tensor([c0.data_ptr()], dtype=torch.int64, device=engine.device)
+        self.src = torch.tensor([c0.data_ptr() + b * c0.stride(0) * self.elem
+                                 for b in range(max_prompts)], dtype=torch.int64,
+                                device=engine.device)
+        self.first = torch.empty(max_prompts, dtype=torch.long, device=engine.device)
         self.stats: list[dict] = []
 
     @torch.inference_mode()
     def run(self, requests: list[Request], prefix: str, t0: float, device_ids: dict | None = None):
         """Serves this prefill group's share of `requests` (group and index set) in arrival
         order; `prefix` namespaces the store keys of this run. device_ids optionally maps
-        rid -> a device-resident [1, L] id tensor (otherwise ids come from pinned host memory)."""
+        rid -> a device-resident [1, L] id tensor (otherwise ids come from pinned host memory).
+        Every pass takes the requests that have arrived, up to max_tokens tokens and
+        max_prompts prompts (all TP ranks of the group take the same ones: their decisions
+        depend only on arrival times, which they read against the same start)."""
         mine = [r for r in requests if self.split.feeder(r.group) == self.g]
         mine.sort(key=lambda r: (r.arrival, r.rid))
         for ring in self.rings.values():  # the previous run ended with every region consumed
@@ -223,37 +232,76 @@ class PrefillWorker:
         m, eng = self.eng.model, self.eng
         dev = eng.device
         n = m.n_layer
-        for r in mine:
+        tp = self.split.tp
+        i = 0
+        while i < len(mine):
             now = time.monotonic() - t0
-            if r.arrival > now:
-                time.sleep(r.arrival - now)
-            L = len(r.prompt)
-            if L >= self.cap:
-                raise ValueError(f"prompt of {L} tokens exceeds the prefill capacity {self.cap - 1}")
+            if mine[i].arrival > now:
+                time.sleep(mine[i].arrival - now)
+                now = time.monotonic() - t0
+            if tp > 1:
+                # The group's ranks must batch the same requests: the first rank's clock decides.
+                now = self._agree(now)
+            # A pass reserves ring space for all its requests before publishing any of them, so
+            # its bytes per ring stay within half the ring: a reservation then only ever waits
+            # for regions of earlier, already published passes.
+            j, tok, per_ring = i, 0, {}
+            while j < len(mine) and j - i < self.max_prompts:
+                r = mine[j]
+                nb = n * len(r.prompt) * eng.row_bytes + ALIGN
+                if j > i and (r.arrival > now or tok + len(r.prompt) > self.max_tokens
+                              or per_ring.get(r.group, 0) + nb > self.rings[r.group].size // 2):
+                    break
+                tok += len(r.prompt)
+                per_ring[r.group] = per_ring.get(r.group, 0) + nb
+                j += 1
+            batch = mine[i:j]
+            for r in batch:
+                if len(r.prompt) > self.cap:
+                    raise ValueError(f"prompt of {len(r.prompt)} tokens exceeds the prefill "
+                                     f"capacity {self.cap}")
             start = time.monotonic() - t0
-            rdy, _ = _keys(prefix, r.group, self.t, r.index)
-            off = self.rings[r.group].reserve(
-                r.index, n * L * eng.row_bytes,
-                lambda k: self.store.wait([_keys(prefix, r.group, self.t, k)[1]]))
-            ids = device_ids[r.rid] if device_ids else torch.tensor(
-                [r.prompt], dtype=torch.long).pin_memory().to(dev, non_blocking=True)
-            st = CacheState(self.cap, key_value_memory_dict=self.cache)
-            tok = m.next_tokens(ids.view(1, L), inference_params=st)
-            live = torch.tensor([L], dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
-            offs = torch.tensor([off], dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            offs = [self.rings[r.group].reserve(
+                r.index, n * len(r.prompt) * eng.row_bytes,
+                lambda k, r=r: self.store.wait([_keys(prefix, r.group, self.t, k)[1]]))
+                for r in batch]
+            lens = [len(r.prompt) for r in batch]
+            if device_ids:
+                ids = torch.cat([device_ids[r.rid].view(-1) for r in batch])
+            else:
+                ids = torch.tensor([t for r in batch for t in r.prompt],
+                                   dtype=torch.long).pin_memory().to(dev, non_blocking=True)
+            live = torch.tensor(lens, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            dst = torch.tensor(offs, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            m.prefill_packed(ids, lens, self.cache, list(range(len(batch))),
+                             out=self.first[:len(batch)])
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            ops.kv_pack(self.src, live, offs, n, self.layer_stride, self.row_stride, eng.row_bytes,
-                        L, self.remotes[r.group])
+            for b, r in enumerate(batch):
+                ops.kv_pack(self.src[b:b + 1], live[b:b + 1], dst[b:b + 1], n, self.layer_stride,
+                            self.row_stride, eng.row_bytes, lens[b], self.remotes[r.group])
             e1.record()
-            # The pack has completed (its peer stores have landed) before the key is published.
+            # Every pack has completed (its peer stores have landed) before a key is published.
             torch.cuda.current_stream().synchronize()
-            first = int(tok)
+            firsts = self.first[:len(batch)].tolist()
             ready = time.monotonic() - t0
-            self.store.set(rdy, json.dumps({"tok": first, "L": L, "off": off}))
-            self.stats.append({"rid": r.rid, "arrival": r.arrival, "start": start, "ready": ready,
-                               "kv_bytes": n * L * eng.row_bytes, "kv_ms": e0.elapsed_time(e1)})
+            kv_ms = e0.elapsed_time(e1)
+            kv_bytes = n * sum(lens) * eng.row_bytes
+            for b, r in enumerate(batch):
+                self.store.set(_keys(prefix, r.group, self.t, r.index)[0],
+                               json.dumps({"tok": firsts[b], "L": lens[b], "off": offs[b]}))
+                self.stats.append({"rid": r.rid, "arrival": r.arrival, "start": start,
+                                   "ready": ready, "kv_bytes": n * lens[b] * eng.row_bytes,
+                                   "kv_ms": kv_ms * lens[b] / sum(lens), "batch": len(batch),
+                                   "pass_kv_bytes": kv_bytes, "pass_kv_ms": kv_ms})
+            i = j
+
+    def _agree(self, now: float) -> float:
+        t = torch.tensor([now], dtype=torch.float64, device=self.eng.device)
+        dist.broadcast(t, src=self.split.prefill_ranks(self.g)[0],
+                       group=self.eng.model.process_group)
+        return float(t.item())
 
 
 class DecodeWorker:

@@ -276,3 +276,55 @@ def test_tp4_shards_on_one_gpu_match_oracle(hx, tmp_path):
     torch.cuda.empty_cache()
     _judge("llama70b-width-4L-tp4-gloo-1gpu", res["tokens"], res["rows"], state, LLAMA70B_4L,
            res["prompt"], extra={"tp": 4, "next_tokens_agree_steps": len(res["agree"])})
+
+
+# ------------------------------------------------------------------------------------------
+# 4. packed (variable-length) prefill
+# ------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", list(DTYPES))
+def test_packed_prefill_matches_reference_golden(hx, golden, fixture_dir, dtype):
+    """All golden prompts prefilled in ONE packed pass (GPTLMHeadModel.prefill_packed): every
+    prompt's last-token logits equal the reference's golden prefill logits (1e-4 f32, 2e-2
+    bf16/f16), its greedy token the reference's first token (f32), and in f32 its layer-0 KV
+    rows the reference's cache values."""
+    from tests.conftest import from_bits
+    dt = DTYPES[dtype]
+    tol = 1e-4 if dt == torch.float32 else 2e-2
+    eng = hx.Engine(fixture_dir, device="cuda", dtype=dtype)
+    rows = golden["engine"][dtype]
+    lens = [len(r["prompt"]) for r in rows]
+    ids = torch.tensor([t for r in rows for t in r["prompt"]], dtype=torch.long, device="cuda")
+    cache = eng.model.allocate_inference_cache(len(rows), max(lens) + 1)
+    logits = eng.model.prefill_packed(ids, lens, cache, list(range(len(rows))), greedy=False)
+    firsts = eng.model.prefill_packed(ids, lens, cache, list(range(len(rows))))
+    for b, row in enumerate(rows):
+        expected = from_bits(row["prefill_logits"], dt).float()
+        torch.testing.assert_close(logits[b].float().cpu(), expected, rtol=0, atol=tol, msg=row["name"])
+        if dt == torch.float32:
+            assert int(firsts[b]) == row["first_token"], row["name"]
+            if row["kv_layer0_values"] is not None:
+                want = from_bits(row["kv_layer0_values"], torch.float32)
+                got = cache[0][b, :lens[b]].cpu().flatten()
+                torch.testing.assert_close(got, want, rtol=0, atol=1e-5, msg=row["name"])
+    assert hx.ops.device_error() == 0
+
+
+def test_packed_prefill_equals_single_prompt_forward_7b_width(hx):
+    """Llama-2-7B widths (2 layers, bf16): ragged prompts in one packed pass give each prompt the
+    logits and greedy token of its own single-prompt forward (up to the projections' summation
+    order: 2e-2), and the caches its decode continues from."""
+    cfg = dict(LLAMA7B, num_hidden_layers=2)
+    eng = hx.Engine.from_config(cfg, dtype="bfloat16", seed=21)
+    g = torch.Generator().manual_seed(3)
+    lens = [300, 17, 1, 129, 900]
+    prompts = [torch.randint(0, 32000, (L,), generator=g).tolist() for L in lens]
+    ids = torch.tensor([t for p in prompts for t in p], dtype=torch.long, device="cuda")
+    cache = eng.model.allocate_inference_cache(len(lens), max(lens) + 8)
+    logits = eng.model.prefill_packed(ids, lens, cache, list(range(len(lens))), greedy=False)
+    for b, p in enumerate(prompts):
+        first, single_cache, single = eng.prefill(p, 8)
+        torch.testing.assert_close(logits[b].float().cpu(), single[0].float().cpu(), rtol=2e-2, atol=2e-2)
+        for i in range(2):
+            torch.testing.assert_close(cache[i][b, :lens[b]].float().cpu(),
+                                       single_cache[i][0].float().cpu(), rtol=2e-2, atol=2e-2)
+    assert hx.ops.device_error() == 0
