@@ -310,9 +310,12 @@ def test_packed_prefill_matches_reference_golden(hx, golden, fixture_dir, dtype)
 
 
 def test_packed_prefill_equals_single_prompt_forward_7b_width(hx):
-    """Llama-2-7B widths (2 layers, bf16): ragged prompts in one packed pass give each prompt the
-    logits and greedy token of its own single-prompt forward (up to the projections' summation
-    order: 2e-2), and the caches its decode continues from."""
+    """Llama-2-7B widths (2 layers, bf16): ragged prompts in one packed pass against each
+    prompt's own single-prompt forward and the f32 truth of the reference's algorithm. The two
+    bf16 paths tile their projection GEMMs differently (M = one prompt vs the sum), so their
+    logits differ by bf16 noise; the bar is the full-depth one: the packed logits are as close to
+    the truth as the single-prompt ones (max error within max(2e-2, 1.5x), mean within 1.5x),
+    and the greedy tokens agree except at near-ties of the truth. The caches agree to that noise."""
     cfg = dict(LLAMA7B, num_hidden_layers=2)
     eng = hx.Engine.from_config(cfg, dtype="bfloat16", seed=21)
     g = torch.Generator().manual_seed(3)
@@ -320,11 +323,26 @@ def test_packed_prefill_equals_single_prompt_forward_7b_width(hx):
     prompts = [torch.randint(0, 32000, (L,), generator=g).tolist() for L in lens]
     ids = torch.tensor([t for p in prompts for t in p], dtype=torch.long, device="cuda")
     cache = eng.model.allocate_inference_cache(len(lens), max(lens) + 8)
-    logits = eng.model.prefill_packed(ids, lens, cache, list(range(len(lens))), greedy=False)
+    packed = eng.model.prefill_packed(ids, lens, cache, list(range(len(lens))), greedy=False).float().cpu()
+    state = {k: v.cpu() for k, v in eng.model.state_dict().items()}
+    truth = OracleModel(LlamaShape.from_hf(cfg), state, torch.float32, attention="flash")
+    e_p, e_s = [], []
     for b, p in enumerate(prompts):
         first, single_cache, single = eng.prefill(p, 8)
-        torch.testing.assert_close(logits[b].float().cpu(), single[0].float().cpu(), rtol=2e-2, atol=2e-2)
-        for i in range(2):
-            torch.testing.assert_close(cache[i][b, :lens[b]].float().cpu(),
-                                       single_cache[i][0].float().cpu(), rtol=2e-2, atol=2e-2)
+        t = truth.forward(torch.tensor([p]), None, last_token_only=True)[0].float()
+        e_p.append((packed[b] - t).abs())
+        e_s.append((single[0].float().cpu() - t).abs())
+        if int(packed[b].argmax()) != int(single[0].argmax()):
+            top = t.topk(2).values
+            assert float(top[0] - top[1]) <= 2 * max(2e-2, float(e_s[-1].max())), b
+        torch.testing.assert_close(cache[0][b, :lens[b]].float().cpu(), single_cache[0][0].float().cpu(),
+                                   rtol=2 ** -6, atol=1e-2)
+        torch.testing.assert_close(cache[1][b, :lens[b]].float().cpu(), single_cache[1][0].float().cpu(),
+                                   rtol=5e-2, atol=5e-2)
+    ep, es = torch.stack(e_p), torch.stack(e_s)
+    _report("packed-prefill-7b-width-2L", max_err_packed_vs_truth=ep.max().item(),
+            max_err_single_vs_truth=es.max().item(), mean_err_packed=ep.mean().item(),
+            mean_err_single=es.mean().item())
+    assert ep.max().item() <= max(2e-2, 1.5 * es.max().item())
+    assert ep.mean().item() <= 1.5 * es.mean().item() + 1e-4
     assert hx.ops.device_error() == 0
