@@ -240,6 +240,98 @@ def roofline_entries(times: dict, work: dict, pk: dict) -> dict:
     return out
 
 
+def prefill_class_times(eng, cache, lens: list[int], reps: int = 3) -> dict:
+    """Tensor-core classes of ONE packed prefill pass (the bench's first pass: its prompts'
+    rows concatenated, at most 8192), each class alone in a CUDA graph of its launches in pass
+    order, CUDA events around replays:
+      gemm_prefill:      the four projections of every layer over all rows of the pass
+                         (flops = 2 x rows x layer weights x layers);
+      prefill_attention: causal attention of every prompt of the pass in every layer, over the
+                         bench's own cache (flops = 4 x hq x d x L^2 / 2 per prompt and layer).
+    Returns {class: (ms, launches, flops)}."""
+    from hexgen2_b200 import ops
+    from hexgen2_b200.engine import PREFILL_PROMPTS, PREFILL_TOKENS
+    m = eng.model
+    dev, dt = eng.device, eng.dtype
+    n, T = 0, 0
+    while n < len(lens) and n < PREFILL_PROMPTS and (n == 0 or T + lens[n] <= PREFILL_TOKENS):
+        T += lens[n]
+        n += 1
+    plens = lens[:n]
+    h, hq, hk, d = m.hidden, m.hq, m.hk, m.head_dim
+    layers = m.transformer.layers
+    I2 = layers[0].mlp.fc1.weight.shape[0]
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def rnd(*size):
+        return (torch.randn(*size, generator=g, device=dev, dtype=torch.float32) * 0.5).to(dt)
+
+    normed, res, ctx, act = rnd(T, h), rnd(T, h), rnd(T, hq * d), rnd(T, I2 // 2)
+    qkv = torch.empty(T, layers[0].mixer.Wqkv.weight.shape[0], device=dev, dtype=dt)
+    tmp = torch.empty(T, h, device=dev, dtype=dt)
+    q = rnd(T, hq, d)
+    out = torch.empty(T, hq, d, device=dev, dtype=dt)
+    zero = torch.zeros(1, dtype=torch.int32, device=dev)
+    offs = [0]
+    for L in plens:
+        offs.append(offs[-1] + L)
+
+    def gemms():
+        for layer in layers:
+            ops.gemm(normed, layer.mixer.Wqkv.weight, out=qkv)
+            ops.gemm(ctx, layer.mixer.out_proj.weight, ops.HX_EPI_RESIDUAL, residual=res, out=tmp)
+            ops.gemm(normed, layer.mlp.fc1.weight, ops.HX_EPI_SWIGLU, out=act)
+            ops.gemm(act, layer.mlp.fc2.weight, ops.HX_EPI_RESIDUAL, residual=res, out=tmp)
+
+    def attention():
+        for i in range(len(layers)):
+            for b, L in enumerate(plens):
+                o = offs[b]
+                ops.prefill_attention(q[o:o + L].view(1, L, hq, d), cache[i], zero, hk, m.scale,
+                                      causal=True, out=out[o:o + L].view(1, L, hq, d),
+                                      batch_offset=b)
+
+    flops = {"gemm_prefill": 2 * T * len(layers) * sum(w.numel() for w in (
+                 layers[0].mixer.Wqkv.weight, layers[0].mixer.out_proj.weight,
+                 layers[0].mlp.fc1.weight, layers[0].mlp.fc2.weight)),
+             "prefill_attention": len(layers) * sum(4 * hq * d * L * L / 2 for L in plens)}
+    res_t = {}
+    for name, fn in (("gemm_prefill", gemms), ("prefill_attention", attention)):
+        fn()
+        torch.cuda.synchronize()
+        before = ops.LAUNCHES
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        launches = ops.LAUNCHES - before
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res_t[name] = (e0.elapsed_time(e1) / reps, launches, flops[name])
+        del graph
+    return res_t, n, T
+
+
+def prefill_roofline_entries(times: dict, prompts: int, rows: int, pk: dict) -> dict:
+    out = {}
+    for name, (ms, launches, flops) in times.items():
+        achieved = flops / (ms / 1e3) / 1e12
+        out[name] = {"kernel": name, "bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None,
+                     "algorithmic_flops": int(flops),
+                     "per": f"one packed prefill pass: {prompts} prompts, {rows} rows ({launches} launches)",
+                     "ms": round(ms, 4), "peak_source": pk["source"] + " (burst cuBLAS bf16, of measured)",
+                     "timing": ("CUDA events around replays of a graph of the pass's launches of "
+                                "this class alone (no event between kernels)")}
+    return out
+
+
 def prefill_latency(eng, lengths=(512, 1024), reps=5) -> dict:
     """Isolated per-request prefill latency (batch 1, prompt ids already on the device, to the
     greedy first token on the device), median of `reps` CUDA-event timings after a warm-up."""
@@ -342,6 +434,8 @@ def run_native_single(args) -> dict:
         roofline = dict(max(roofs.values(), key=lambda r: r["ms"]))
         roofline["decode_step_ms_in_situ"] = round(dec_step_ms, 4)
         roofline["classes_sum_ms"] = round(sum(r["ms"] for r in roofs.values()), 4)
+        ptimes, pn, prow = prefill_class_times(eng, cache, lens)
+        roofs.update(prefill_roofline_entries(ptimes, pn, prow, pk))
 
     # End to end through the public API: pinned host prompts in, host token lists out.
     e2e = run_e2e(eng, prompts, out_len, args) if args.e2e_steps > 0 else None
