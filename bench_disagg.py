@@ -168,12 +168,15 @@ def run_serving(args, bench) -> dict | None:
 
     phase(warm, "w", device_ids)
     worker.stats.clear()
+    if kind == "decode":
+        worker.step_times.clear()
     ops.LAUNCHES = 0
     with bench.ClockSampler(local, enabled=args.clocks) as clocks:
         outputs, dev_ms, _ = phase(timed, "t", device_ids)
     launches = ops.LAUNCHES
     stats = list(worker.stats)
     steps_done = getattr(worker, "steps", 0)
+    step_times = list(getattr(worker, "step_times", []))
     tokens_ok = _check_tokens(outputs, timed) if kind == "decode" else None
 
     # End to end: prompts from pinned host memory to host token lists (wall clock, max over ranks).
@@ -202,7 +205,8 @@ def run_serving(args, bench) -> dict | None:
     launches_all = int(_sum([launches])[0])
     gathered = [None] * world
     dist.all_gather_object(gathered, {"kind": kind, "stats": stats, "clocks": clocks.summary(),
-                                      "roofs": roofs, "steps": steps_done, "tokens_ok": tokens_ok})
+                                      "roofs": roofs, "steps": steps_done, "tokens_ok": tokens_ok,
+                                      "step_times": _step_summary(step_times)})
     for h in handoffs:
         h.close()
     torch.cuda.synchronize()
@@ -213,6 +217,18 @@ def run_serving(args, bench) -> dict | None:
     if rank != 0:
         return None
     return _serving_line(args, bench, split, cfg, timed, gathered, dev_max, launches_all, e2e, poisson)
+
+
+def _step_summary(times):
+    """p50 / p90 of a decode rank's host time per decode step: control (store, admissions) and
+    the step itself (graph replay until the tokens are read back), and the mean active slots."""
+    if not times:
+        return None
+    ctrl = [1e3 * t[0] for t in times]
+    step = [1e3 * t[1] for t in times]
+    return {"steps": len(times), "control_ms_p50": _pct(ctrl, 0.5), "control_ms_p90": _pct(ctrl, 0.9),
+            "step_ms_p50": _pct(step, 0.5), "step_ms_p90": _pct(step, 0.9),
+            "active_slots_mean": round(sum(t[2] for t in times) / len(times), 2)}
 
 
 def _check_tokens(outputs, timed):
@@ -263,6 +279,7 @@ def _serving_line(args, bench, split, cfg, timed, gathered, dev_max, launches, e
         "prefill_latency_ms": {"p50": _pct(prefill_ms, 0.5), "p90": _pct(prefill_ms, 0.9)},
         "request_latency_ms": {"p50": _pct(lat_ms, 0.5), "p90": _pct(lat_ms, 0.9)},
         "decode_steps_max_rank": steps,
+        "decode_step_host_ms": [g["step_times"] for g in dec_ranks if g["step_times"]][:2],
         "kv_transfer_gbs_per_pair": round(kv_med, 1) if kv_med else None,
         "kv_roofline": None if not kv_med else {
             "kernel": "kv_pack (peer stores over NVLink, one request per launch)", "bound": "nvlink",

@@ -315,6 +315,7 @@ class DecodeWorker:
         self.batcher = ContinuousBatcher(engine, slots, capacity)
         self.stats: list[dict] = []
         self.steps = 0
+        self.step_times: list[tuple] = []  # (control s, step s, active slots) per decode step
 
     @torch.inference_mode()
     def run(self, requests: list[Request], prefix: str, t0: float, poll_s: float = 0.0005):
@@ -328,6 +329,7 @@ class DecodeWorker:
         done, step = 0, 0
         admitted_at = {}
         while done < len(mine):
+            t_loop = time.perf_counter()
             adm = []
             if leader:
                 free = len(b.free_slots())
@@ -351,8 +353,12 @@ class DecodeWorker:
                     self.stats.append({"rid": rid, "tokens": 1, "done": admitted_at[rid],
                                        "admitted": admitted_at[rid]})
             if b.active():
+                t_step = time.perf_counter()
                 finished = b.step()
                 self.steps += 1
+                # Host wall time per decode iteration: control (store, admissions) and the step
+                # (graph replay up to the tokens read back).
+                self.step_times.append((t_step - t_loop, time.perf_counter() - t_step, b.active()))
             else:
                 finished = []
                 if adm:
