@@ -42,6 +42,10 @@ _SIGNATURES = {
     "hx_prefill_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
                                      c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_float,
                                      c_void_p, c_int, c_void_p]),
+    "hx_prefill_attention_varlen": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                            c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                            c_int64, c_int64, c_int64, c_int64, c_int64, c_int,
+                                            c_float, c_void_p, c_int, c_void_p]),
     "hx_decode_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64,
                                     c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
                                     c_void_p, c_size_t, c_int, c_void_p]),

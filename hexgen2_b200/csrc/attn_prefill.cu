@@ -171,6 +171,32 @@ int prefill_attention_tc(const void* q, const void* cache, int64_t cbs, int64_t 
                          int64_t d, int causal, float scale, void* out, int dtype,
                          cudaStream_t stream);
 
+int prefill_attention_tc_varlen(const void* q, const void* cache, int64_t cbs, int64_t css,
+                                int64_t cache_rows, const int32_t* seq_off, const int32_t* slots,
+                                const int32_t* pos_start, const int32_t* items,
+                                int64_t n_prompts, int64_t n_items, int64_t total_rows,
+                                int64_t hq, int64_t hk, int64_t d, int causal, float scale,
+                                void* out, int dtype, cudaStream_t stream);
+
+extern "C" int hx_prefill_attention_varlen(
+    const void* q, const void* cache, int64_t cache_batch_stride, int64_t cache_seq_stride,
+    int64_t cache_rows, const int32_t* seq_offsets, const int32_t* slots,
+    const int32_t* pos_start, const int32_t* items, int64_t n_prompts, int64_t n_items,
+    int64_t total_rows, int64_t n_heads, int64_t n_heads_kv, int64_t head_dim, int causal,
+    float softmax_scale, void* out, int dtype, void* stream) {
+  HX_REQUIRE(q && cache && seq_offsets && slots && pos_start && items && out,
+             "hx_prefill_attention_varlen: null pointer");
+  HX_REQUIRE(n_heads_kv > 0 && n_heads % n_heads_kv == 0, "hx_prefill_attention_varlen: bad heads");
+  HX_REQUIRE(cache_seq_stride >= 2 * n_heads_kv * head_dim && cache_rows > 0 && n_prompts >= 0 &&
+                 n_items >= 0 && total_rows >= 0,
+             "hx_prefill_attention_varlen: bad sizes");
+  if (n_prompts == 0 || n_items == 0 || total_rows == 0) return HX_OK;
+  return prefill_attention_tc_varlen(q, cache, cache_batch_stride, cache_seq_stride, cache_rows,
+                                     seq_offsets, slots, pos_start, items, n_prompts, n_items,
+                                     total_rows, n_heads, n_heads_kv, head_dim, causal,
+                                     softmax_scale, out, dtype, (cudaStream_t)stream);
+}
+
 extern "C" int hx_prefill_attention(const void* q, const void* cache, int64_t cache_batch_stride,
                                     int64_t cache_seq_stride, int64_t cache_batch_offset,
                                     const int32_t* pos_start, int64_t batch, int64_t seqlen_q,

@@ -58,6 +58,13 @@ struct PAArgs {
   void* out;
   const int32_t* pos_start;
   int64_t cache_batch_offset;
+  // Variable-length launches (items != nullptr): the queries of n_prompts prompts are packed
+  // row after row; prompt b owns q/out rows [seq_off[b], seq_off[b + 1]) and cache row
+  // slots[b]; grid.y enumerates work items (prompt, query block), heaviest first.
+  const int2* items;
+  const int32_t* seq_off;
+  const int32_t* slots;
+  int n_prompts;
 };
 
 template <typename T, int D>
@@ -85,8 +92,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Heads vary fastest and query blocks run last-to-first, so under a causal mask the CTAs with
   // the most key tiles start in the first wave and the light ones fill the tail.
-  const int h = blockIdx.x, qblk = gridDim.y - 1 - blockIdx.y, b = blockIdx.z;
-  const int S = a.seqlen_q;
+  const int h = blockIdx.x;
+  int qblk, b, S;
+  int64_t row0, bb;
+  if (a.items) {
+    const int2 it = a.items[blockIdx.y];
+    b = it.x;
+    qblk = it.y;
+    if (b < 0 || b >= a.n_prompts) {  // the whole CTA leaves before any barrier or allocation
+      if (threadIdx.x == 0) record_device_error(HX_DEVERR_BAD_ARGUMENT);
+      return;
+    }
+    row0 = a.seq_off[b];
+    S = a.seq_off[b + 1] - a.seq_off[b];
+    bb = a.slots[b];
+    if (qblk < 0 || qblk * kRows >= S) {
+      if (threadIdx.x == 0) record_device_error(HX_DEVERR_BAD_ARGUMENT);
+      return;
+    }
+  } else {
+    qblk = gridDim.y - 1 - blockIdx.y;
+    b = blockIdx.z;
+    S = a.seqlen_q;
+    row0 = (int64_t)b * S;
+    bb = a.cache_batch_offset + b;
+  }
   const int q0 = qblk * kRows;
   const int nq = min(kRows, S - q0);
   const int p0 = a.pos_start[b];
@@ -127,8 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, L::kChunks * kChunkBytes);
       for (int c = 0; c < L::kChunks; ++c)
-        tma_load_3d(sm + L::kQ + c * kChunkBytes, &tmQ, q_full, c * 64, h, b * S + q0);
-      const int bb = (int)(a.cache_batch_offset + b);
+        tma_load_3d(sm + L::kQ + c * kChunkBytes, &tmQ, q_full, c * 64, h, (int)(row0 + q0));
       uint32_t k_issued = 0, v_issued = 0;
       // Step i loads K_i, then V_{i-1}: the MMA thread's order is S_0, S_1, PV_0, S_2, PV_1, ...
       for (int i = 0; i <= n_tiles; ++i) {
@@ -138,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&k_full[st], L::kTile);
           uint8_t* kb = sm + L::kK0 + st * L::kTile;
           for (int c = 0; c < L::kChunks; ++c)
-            tma_load_4d(kb + c * kChunkBytes, &tmKV, &k_full[st], c * 64, hk, i * kRows, bb);
+            tma_load_4d(kb + c * kChunkBytes, &tmKV, &k_full[st], c * 64, hk, i * kRows, (int)bb);
           ++k_issued;
         }
         if (i >= 1) {
@@ -148,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* vb = sm + L::kV0 + st * L::kTile;
           for (int c = 0; c < L::kChunks; ++c)
             tma_load_4d(vb + c * kChunkBytes, &tmKV, &v_full[st], c * 64, a.n_heads_kv + hk,
-                        t * kRows, bb);
+                        t * kRows, (int)bb);
           ++v_issued;
         }
       }
@@ -363,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float l_tot = l_run + red[(half ^ 1) * kRows + r];
       tc_fence_after();
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-      T* orow = reinterpret_cast<T*>(a.out) + (((int64_t)b * S + q0 + r) * a.n_heads + h) * D + half * kOHalf;
+      T* orow = reinterpret_cast<T*>(a.out) + ((row0 + q0 + r) * a.n_heads + h) * D + half * kOHalf;
 #pragma unroll 1
       for (int c = 0; c < kOHalf / 32; ++c) {
         uint32_t o[32];
@@ -434,14 +463,84 @@ int launch_tc(const void* q, const void* cache, int64_t cbs, int64_t css, int64_
     if (s) return s;
     attr[dev & 63] = true;
   }
-  PAArgs args{(int)S, (int)hq, (int)hk, causal, scale * 1.4426950408889634f, out, pos_start, cbo};
+  PAArgs args{(int)S, (int)hq, (int)hk, causal, scale * 1.4426950408889634f, out, pos_start, cbo,
+              nullptr, nullptr, nullptr, 0};
   dim3 grid((unsigned)hq, ceil_div(S, kRows), (unsigned)B);
   kern<<<grid, kThreads, L::kSmem, stream>>>(mq, mkv, args);
   HX_LAUNCH_CHECK("prefill_attn_tc_kernel");
   return HX_OK;
 }
 
+// Variable-length launch: one grid over (head, work item) for all prompts of a packed pass.
+template <typename T, int D>
+int launch_tc_varlen(const void* q, const void* cache, int64_t cbs, int64_t css,
+                     int64_t cache_rows, const int32_t* seq_off, const int32_t* slots,
+                     const int32_t* pos_start, const int32_t* items, int64_t n_prompts,
+                     int64_t n_items, int64_t total_rows, int64_t hq, int64_t hk, int causal,
+                     float scale, void* out, int dtype, cudaStream_t stream) {
+  using L = Lay<D>;
+  CUtensorMap mq, mkv;
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)hq, (uint64_t)total_rows};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)hq * D * 2};
+    const uint32_t box[3] = {64, 1, (uint32_t)kRows};
+    int s = make_tensor_map(&mq, q, 3, dims, strides, box, dtype);
+    if (s) return s;
+  }
+  {
+    const int64_t max_seq = cbs / css;
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)(2 * hk), (uint64_t)max_seq,
+                              (uint64_t)cache_rows};
+    const uint64_t strides[3] = {(uint64_t)D * 2, (uint64_t)css * 2, (uint64_t)cbs * 2};
+    const uint32_t box[4] = {64, 1, (uint32_t)kRows, 1};
+    int s = make_tensor_map(&mkv, cache, 4, dims, strides, box, dtype);
+    if (s) return s;
+  }
+  auto kern = prefill_attn_tc_kernel<T, D>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    int s = hx::cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)L::kSmem),
+                            "cudaFuncSetAttribute(prefill_attn_tc)");
+    if (s) return s;
+    attr[dev & 63] = true;
+  }
+  PAArgs args{0, (int)hq, (int)hk, causal, scale * 1.4426950408889634f, out, pos_start, 0,
+              reinterpret_cast<const int2*>(items), seq_off, slots, (int)n_prompts};
+  dim3 grid((unsigned)hq, (unsigned)n_items, 1);
+  kern<<<grid, kThreads, L::kSmem, stream>>>(mq, mkv, args);
+  HX_LAUNCH_CHECK("prefill_attn_tc_kernel (varlen)");
+  return HX_OK;
+}
+
 }  // namespace
+
+// Variable-length tensor-core prefill attention (bf16/f16, head_dim 64/128); returns
+// HX_ERR_UNSUPPORTED for other shapes so the caller can attend prompt by prompt.
+int prefill_attention_tc_varlen(const void* q, const void* cache, int64_t cbs, int64_t css,
+                                int64_t cache_rows, const int32_t* seq_off, const int32_t* slots,
+                                const int32_t* pos_start, const int32_t* items,
+                                int64_t n_prompts, int64_t n_items, int64_t total_rows,
+                                int64_t hq, int64_t hk, int64_t d, int causal, float scale,
+                                void* out, int dtype, cudaStream_t stream) {
+  if ((dtype != HX_BF16 && dtype != HX_F16) || (d != 64 && d != 128)) return HX_ERR_UNSUPPORTED;
+  if (css % 8 || css <= 0 || cbs % css || ((uintptr_t)q % 16) || ((uintptr_t)cache % 16) ||
+      total_rows > INT32_MAX || n_items > 65535)
+    return HX_ERR_UNSUPPORTED;
+#define HX_PA_VARLEN(TT, DD)                                                                  \
+  return launch_tc_varlen<TT, DD>(q, cache, cbs, css, cache_rows, seq_off, slots, pos_start,   \
+                                  items, n_prompts, n_items, total_rows, hq, hk, causal, scale, \
+                                  out, dtype, stream)
+  if (dtype == HX_BF16) {
+    if (d == 128) HX_PA_VARLEN(__nv_bfloat16, 128);
+    HX_PA_VARLEN(__nv_bfloat16, 64);
+  }
+  if (d == 128) HX_PA_VARLEN(__half, 128);
+  HX_PA_VARLEN(__half, 64);
+#undef HX_PA_VARLEN
+}
 
 // Tensor-core prefill attention; returns HX_ERR_UNSUPPORTED for shapes it does not cover so
 // the caller can use the CUDA-core kernel (f32, head_dim 32, unaligned strides).

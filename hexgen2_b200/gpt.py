@@ -435,6 +435,7 @@ class GPTLMHeadModel(nn.Module):
         q = torch.empty(T, hq, d, dtype=dtype, device=device)
         ctx = torch.empty(T, hq, d, dtype=dtype, device=device)
         layers = self.transformer.layers
+        meta = ops.varlen_meta(lengths, slots, device)
         if self.tp == 1:
             ops.embed_rmsnorm(ids, w_emb, layers[0].norm1.weight, self.eps, residual, normed)
         else:
@@ -449,9 +450,15 @@ class GPTLMHeadModel(nn.Module):
                 ops.rotary_cache_write(qkv[o:o + L], 1, L, hq, hk, d, zero, cos, sin, cache,
                                        q_out=q[o:o + L].view(1, L, hq, d), batch_offset=slots[b],
                                        interleaved=mixer.rotary_emb_interleaved)
-                ops.prefill_attention(q[o:o + L].view(1, L, hq, d), cache, zero, hk, self.scale,
-                                      causal=True, out=ctx[o:o + L].view(1, L, hq, d),
-                                      batch_offset=slots[b])
+            # All prompts' causal attention in one launch (one grid over heads x 128-query
+            # blocks of every prompt); prompt by prompt where that kernel does not apply.
+            if not ops.prefill_attention_varlen(q, cache, lengths, slots, hk, self.scale, ctx,
+                                                meta=meta):
+                for b in range(n):
+                    o, L = offs[b], lengths[b]
+                    ops.prefill_attention(q[o:o + L].view(1, L, hq, d), cache, zero, hk,
+                                          self.scale, causal=True,
+                                          out=ctx[o:o + L].view(1, L, hq, d), batch_offset=slots[b])
             c2 = ctx.view(T, hq * d)
             if self.tp == 1:
                 ops.gemm(c2, mixer.out_proj.weight, HX_EPI_RESIDUAL, residual=residual, out=residual)

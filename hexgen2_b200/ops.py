@@ -188,6 +188,46 @@ def prefill_attention(q, cache, pos_start, n_heads_kv, softmax_scale, causal=Tru
     return out
 
 
+def varlen_meta(lengths, slots, device):
+    """Device table for prefill_attention_varlen: row offsets [n + 1], cache slots [n], start
+    positions [n] (0: prefill from an empty cache) and the (prompt, 128-query block) work items,
+    heaviest causal work (latest block) first. Returns (table, n_items, items start index)."""
+    n = len(lengths)
+    offs = [0]
+    for L in lengths:
+        offs.append(offs[-1] + L)
+    items = sorted(((b, qb) for b, L in enumerate(lengths) for qb in range(-(-L // 128))),
+                   key=lambda it: (-it[1], it[0]))
+    head = offs + list(slots) + [0] * n
+    if len(head) % 2:
+        head.append(0)  # the (prompt, block) pairs are read as 8-byte int2
+    meta = torch.tensor(head + [v for it in items for v in it], dtype=torch.int32).pin_memory()
+    return meta.to(device, non_blocking=True), len(items), len(head)
+
+
+def prefill_attention_varlen(q, cache, lengths, slots, n_heads_kv, softmax_scale, out,
+                             meta=None) -> bool:
+    """Causal prefill attention of several prompts packed row after row in q [T, hq, d] (prompt
+    b: lengths[b] rows, cache row slots[b], positions from 0) in ONE launch, into out. meta: a
+    varlen_meta table (built here when omitted; build it beforehand for a CUDA-graph capture).
+    Returns False, launching nothing, for shapes the tensor-core kernel does not cover (f32,
+    head_dim 32); the caller then attends prompt by prompt."""
+    _require_cuda(q, cache, out)
+    T, hq, d = q.shape
+    n = len(lengths)
+    table, n_items, items_at = meta if meta is not None else varlen_meta(lengths, slots, q.device)
+    base = table.data_ptr()
+    st = _L().hx_prefill_attention_varlen(
+        _p(q), _p(cache), cache.stride(0), cache.stride(1), cache.shape[0], base,
+        base + 4 * (n + 1), base + 4 * (2 * n + 1), base + 4 * items_at, n, n_items, T, hq,
+        n_heads_kv, d, 1, float(softmax_scale), _p(out), _code(q), _stream())
+    if st == _lib.HX_ERR_UNSUPPORTED:
+        return False
+    check(st, "hx_prefill_attention_varlen")
+    _count(1)
+    return True
+
+
 def decode_attention(q, cache, seqlens, n_heads_kv, max_seqlen, softmax_scale, out=None):
     """q [B, hq, d] against cache[b, :seqlens[b]] (seqlens int32 on device)."""
     _require_cuda(q, cache, seqlens)

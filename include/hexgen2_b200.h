@@ -151,6 +151,21 @@ int hx_prefill_attention(const void* q, const void* cache, int64_t cache_batch_s
                          const int32_t* pos_start, int64_t batch, int64_t seqlen_q,
                          int64_t n_heads, int64_t n_heads_kv, int64_t head_dim, int causal,
                          float softmax_scale, void* out, int dtype, void* stream);
+/* Prefill attention of several prompts packed row after row in one launch (f16/bf16,
+ * head_dim 64/128; HX_ERR_UNSUPPORTED otherwise, so the caller can attend prompt by prompt).
+ * q/out: [total_rows, n_heads, head_dim]; prompt b owns rows [seq_offsets[b], seq_offsets[b+1])
+ * and reads keys/values from cache row slots[b] (of cache_rows rows), positions
+ * 0 : pos_start[b] + its length, with hx_prefill_attention's causal rule. items: n_items pairs
+ * (prompt, 128-query block) of int32, every block of every prompt once, heaviest first for
+ * causal work. All arrays live on the device. Same call site as hx_prefill_attention
+ * (flash_attn_kvpacked_func, mha.py:141/:569), for the packed prefill of several requests. */
+int hx_prefill_attention_varlen(const void* q, const void* cache, int64_t cache_batch_stride,
+                                int64_t cache_seq_stride, int64_t cache_rows,
+                                const int32_t* seq_offsets, const int32_t* slots,
+                                const int32_t* pos_start, const int32_t* items, int64_t n_prompts,
+                                int64_t n_items, int64_t total_rows, int64_t n_heads,
+                                int64_t n_heads_kv, int64_t head_dim, int causal,
+                                float softmax_scale, void* out, int dtype, void* stream);
 
 /* Single-query decode attention, split over the key axis (flash-decoding), GQA aware.
  * q: [batch, n_heads, head_dim]; sequence b attends to cache[b, 0 : seqlens_k[b]]

@@ -451,3 +451,35 @@ def test_decode_gemm_is_deterministic_and_needs_no_workspace(ops, M, N, K):
     torch.testing.assert_close(outs[0].cpu().float(), gemm_ref(a, b, 1, r, dt).float(),
                                rtol=2 ** -6, atol=2e-2)
     assert ops.device_error() == 0
+
+
+# ------------------------------------------------------------------------------ varlen prefill
+@pytest.mark.parametrize("hq,hk,d", [(32, 32, 128), (32, 8, 128), (16, 2, 64)])
+def test_prefill_attention_varlen_equals_per_prompt(ops, hq, hk, d):
+    """Ragged prompts packed row after row (lengths 1, 127, 128, 129, 300, 700; permuted cache
+    slots) in ONE varlen launch give exactly the per-prompt launches' outputs (same kernel work
+    per query block) and match the FlashAttention-numerics oracle within 2e-2."""
+    dt = torch.bfloat16
+    lens = [129, 1, 700, 128, 127, 300]
+    slots = [3, 0, 6, 1, 4, 2]
+    B, cap = 7, 800
+    g = torch.Generator().manual_seed(hq * 10 + d)
+    cache_h = torch.randn(B, cap, 2, hk, d, generator=g).to(dt)
+    q_h = torch.randn(sum(lens), hq, d, generator=g).to(dt)
+    cache, q = cache_h.cuda(), q_h.cuda()
+    scale = d ** -0.5
+    out = torch.full_like(q, float("nan"))
+    assert ops.prefill_attention_varlen(q, cache, lens, slots, hk, scale, out)
+    zero = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o = 0
+    for b, L in enumerate(lens):
+        ref = ops.prefill_attention(q[o:o + L].view(1, L, hq, d), cache, zero, hk, scale,
+                                    causal=True, batch_offset=slots[b])
+        assert torch.equal(out[o:o + L], ref.view(L, hq, d)), b
+        want = flash_attention(q_h[o:o + L][None], cache_h[slots[b], :L][None], True, scale)[0]
+        torch.testing.assert_close(out[o:o + L].float().cpu(), want.float(), rtol=2e-2, atol=2e-2)
+        o += L
+    assert ops.device_error() == 0
+    q32 = q.float()
+    assert not ops.prefill_attention_varlen(q32, cache.float(), lens, slots, hk, scale,
+                                            torch.empty_like(q32))
