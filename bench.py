@@ -244,7 +244,8 @@ def prefill_class_times(eng, cache, lens: list[int], reps: int = 3) -> dict:
     """Tensor-core classes of ONE packed prefill pass (the bench's first pass: its prompts'
     rows concatenated, at most 8192), each class alone in a CUDA graph of its launches in pass
     order, CUDA events around replays:
-      gemm_prefill:      the four projections of every layer over all rows of the pass
+      gemm_prefill:      the four projections of every layer over all rows of the pass, Wqkv
+                         with its rotary + KV-cache write epilogue
                          (flops = 2 x rows x layer weights x layers);
       prefill_attention: causal attention of every prompt of the pass in every layer, over the
                          bench's own cache (flops = 4 x hq x d x L^2 / 2 per prompt and layer).
@@ -267,23 +268,20 @@ def prefill_class_times(eng, cache, lens: list[int], reps: int = 3) -> dict:
         return (torch.randn(*size, generator=g, device=dev, dtype=torch.float32) * 0.5).to(dt)
 
     normed, res, ctx, act = rnd(T, h), rnd(T, h), rnd(T, hq * d), rnd(T, I2 // 2)
-    qkv = torch.empty(T, layers[0].mixer.Wqkv.weight.shape[0], device=dev, dtype=dt)
     tmp = torch.empty(T, h, device=dev, dtype=dt)
     q = rnd(T, hq, d)
     out = torch.empty(T, hq, d, device=dev, dtype=dt)
-    zero = torch.zeros(1, dtype=torch.int32, device=dev)
-    offs = [0]
-    for L in plens:
-        offs.append(offs[-1] + L)
+    meta = ops.varlen_meta(plens, list(range(n)), dev)  # built before the graph capture
+    cos, sin = m.rope_tables(cache[0].shape[1], dev, dt)
 
     def gemms():
-        for layer in layers:
-            ops.gemm(normed, layer.mixer.Wqkv.weight, out=qkv)
+        for i, layer in enumerate(layers):
+            # Wqkv with rotary + the KV-cache write in its epilogue, as the pass runs it.
+            ops.gemm_qkv_rotary_varlen(normed, layer.mixer.Wqkv.weight, plens, list(range(n)),
+                                       hq, hk, d, cos, sin, cache[i], q, meta=meta)
             ops.gemm(ctx, layer.mixer.out_proj.weight, ops.HX_EPI_RESIDUAL, residual=res, out=tmp)
             ops.gemm(normed, layer.mlp.fc1.weight, ops.HX_EPI_SWIGLU, out=act)
             ops.gemm(act, layer.mlp.fc2.weight, ops.HX_EPI_RESIDUAL, residual=res, out=tmp)
-
-    meta = ops.varlen_meta(plens, list(range(n)), dev)  # built before the graph capture
 
     def attention():
         for i in range(len(layers)):
@@ -320,12 +318,17 @@ def prefill_roofline_entries(times: dict, prompts: int, rows: int, pk: dict) -> 
     out = {}
     for name, (ms, launches, flops) in times.items():
         achieved = flops / (ms / 1e3) / 1e12
+        # The pass is timed right after the seconds-long timed steps, at the power-capped
+        # clock those run at, so the denominator is the sustained cuBLAS figure; the burst
+        # fraction is kept beside it.
+        peak = pk["bf16_tflops_sustained"]
         out[name] = {"kernel": name, "bound": "tensor", "achieved": round(achieved, 1),
-                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None,
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "frac_of_burst": round(achieved / pk["bf16_tflops"], 4), "traffic": None,
                      "algorithmic_flops": int(flops),
                      "per": f"one packed prefill pass: {prompts} prompts, {rows} rows ({launches} launches)",
-                     "ms": round(ms, 4), "peak_source": pk["source"] + " (burst cuBLAS bf16, of measured)",
+                     "ms": round(ms, 4),
+                     "peak_source": pk["source"] + " (sustained cuBLAS bf16 under the power cap)",
                      "timing": ("CUDA events around replays of a graph of the pass's launches of "
                                 "this class alone (no event between kernels)")}
     return out

@@ -39,6 +39,11 @@ _SIGNATURES = {
                                    c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
                                    c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                    c_void_p, c_size_t, c_int, c_void_p]),
+    "hx_gemm_qkv_rotary_varlen": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                          c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                                          c_int64, c_int64, c_void_p, c_void_p, c_int64,
+                                          c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                          c_void_p, c_size_t, c_int, c_void_p]),
     "hx_prefill_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
                                      c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_float,
                                      c_void_p, c_int, c_void_p]),

@@ -47,7 +47,37 @@ struct QkvArgs {
   const void* cos;
   const void* sin;
   int n_heads, n_heads_kv, head_dim, seqlen;
+  // Packed prompts (seq_offsets != nullptr): prompt b owns rows [seq_offsets[b],
+  // seq_offsets[b+1]) and cache row slots[b] (< cache_rows); seqlen and cbo are unused.
+  const int32_t* seq_offsets;
+  const int32_t* slots;
+  int n_prompts;
+  int64_t cache_rows;
 };
+
+// Prompt of output row m: m / seqlen for equal-length prompts, else the last b with
+// seq_offsets[b] <= m (binary search; rows past the table's end fall into the last prompt and
+// fail the position bound check).
+HX_DEVICE int qkv_prompt(const QkvArgs& q, int m) {
+  if (!q.seq_offsets) return m / q.seqlen;
+  int lo = 0, hi = q.n_prompts - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (q.seq_offsets[mid] <= m) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+// Cache position of row m of prompt b.
+HX_DEVICE int64_t qkv_pos(const QkvArgs& q, int b, int m) {
+  const int first = q.seq_offsets ? q.seq_offsets[b] : b * q.seqlen;
+  return (int64_t)q.pos_start[b] + (m - first);
+}
+// Cache batch row of prompt b, or -1 when it lies outside the cache.
+HX_DEVICE int64_t qkv_cache_row(const QkvArgs& q, int b) {
+  const int64_t r = q.seq_offsets ? (int64_t)q.slots[b] : q.cbo + b;
+  return r >= 0 && r < q.cache_rows ? r : -1;
+}
 
 struct GemmArgs {
   int M, N, K;
@@ -62,7 +92,7 @@ struct GemmArgs {
 
 HX_DEVICE float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-// Fused Wqkv epilogue for the feature pair (n, n+1), n even, of row m = b * seqlen + s: the
+// Fused Wqkv epilogue for the feature pair (n, n+1), n even, of row m = row s of prompt b: the
 // values are rounded like the reference's Linear output; q and k pairs are rotated (f32 math
 // on the dtype-cached cos/sin, as flash_attn's rotary) and q goes to q_out, k and v to the cache
 // row of position pos_start[b] + s (the packed [k; v] part of a row is exactly the cache's
@@ -71,9 +101,9 @@ template <typename T>
 HX_DEVICE void qkv_store_pair(const GemmArgs& a, int m, int n, float v0, float v1) {
   if (m >= a.M || n >= a.N) return;
   const QkvArgs& q = a.qkv;
-  const int b = m / q.seqlen, s = m - b * q.seqlen;
-  const int64_t pos = (int64_t)q.pos_start[b] + s;
-  if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows) {
+  const int b = qkv_prompt(q, m);
+  const int64_t pos = qkv_pos(q, b, m), row = qkv_cache_row(q, b);
+  if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows || row < 0) {
     record_device_error(HX_DEVERR_BAD_ARGUMENT);
     return;
   }
@@ -89,7 +119,7 @@ HX_DEVICE void qkv_store_pair(const GemmArgs& a, int m, int n, float v0, float v
     x1 = o1;
   }
   T* dst = n < hqd ? reinterpret_cast<T*>(q.q_out) + (int64_t)m * hqd + n
-                   : reinterpret_cast<T*>(q.cache) + (q.cbo + b) * q.cbs + pos * q.css + (n - hqd);
+                   : reinterpret_cast<T*>(q.cache) + row * q.cbs + pos * q.css + (n - hqd);
   T pair[2] = {DT<T>::from_f(x0), DT<T>::from_f(x1)};
   *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(pair);
 }
@@ -106,9 +136,9 @@ HX_DEVICE void epilogue_store(const GemmArgs& a, int m, int n0, const float* v) 
       return;
     }
     // The 32 columns lie in one head: one destination row, 16 consecutive cos/sin entries.
-    const int b = m / q.seqlen, s = m - b * q.seqlen;
-    const int64_t pos = (int64_t)q.pos_start[b] + s;
-    if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows) {
+    const int b = qkv_prompt(q, m);
+    const int64_t pos = qkv_pos(q, b, m), row = qkv_cache_row(q, b);
+    if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows || row < 0) {
       record_device_error(HX_DEVERR_BAD_ARGUMENT);
       return;
     }
@@ -135,7 +165,7 @@ HX_DEVICE void epilogue_store(const GemmArgs& a, int m, int n0, const float* v) 
       for (int j = 0; j < 32; ++j) out[j] = DT<T>::from_f(v[j]);
     }
     T* dst = n0 < hqd ? reinterpret_cast<T*>(q.q_out) + (int64_t)m * hqd + n0
-                      : reinterpret_cast<T*>(q.cache) + (q.cbo + b) * q.cbs + pos * q.css + (n0 - hqd);
+                      : reinterpret_cast<T*>(q.cache) + row * q.cbs + pos * q.css + (n0 - hqd);
 #pragma unroll
     for (int j = 0; j < 32; j += 8)
       *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(out + j);
@@ -477,8 +507,8 @@ HX_DEVICE void sk_store8(const GemmArgs& a, const int (&b)[8], int nr, int n, in
     for (int i = 0; i < 8; ++i) {
       if (!(i < nr && b[i] < a.M)) continue;
       const int m = b[i];
-      const int64_t pos = e.pos[i];
-      if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows) {
+      const int64_t pos = e.pos[i], row = qkv_cache_row(q, qkv_prompt(q, m));
+      if (pos < 0 || pos >= q.max_seq || pos >= q.table_rows || row < 0) {
         record_device_error(HX_DEVERR_BAD_ARGUMENT);
         continue;
       }
@@ -490,9 +520,8 @@ HX_DEVICE void sk_store8(const GemmArgs& a, const int (&b)[8], int nr, int n, in
         x0 = o0;
         x1 = o1;
       }
-      const int bb = m / q.seqlen;
       T* dst = n < hqd ? reinterpret_cast<T*>(q.q_out) + (int64_t)m * hqd + n
-                       : reinterpret_cast<T*>(q.cache) + (q.cbo + bb) * q.cbs + pos * q.css + (n - hqd);
+                       : reinterpret_cast<T*>(q.cache) + row * q.cbs + pos * q.css + (n - hqd);
       T pr2[2] = {DT<T>::from_f(x0), DT<T>::from_f(x1)};
       *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(pr2);
     }
@@ -619,7 +648,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Row positions, loaded while the main loop runs.
       const QkvArgs& q = a.qkv;
       for (int m = threadIdx.x - 64; m < min(BN, a.M); m += 128)
-        pos_s[m] = q.pos_start[m / q.seqlen] + m % q.seqlen;
+        pos_s[m] = (int)qkv_pos(q, qkv_prompt(q, m), m);
       named_bar_sync(2, 128);
     }
     // The first eight rows this CTA stores: their epilogue inputs are fetched while the MMAs
@@ -1384,6 +1413,62 @@ int hx_gemm_qkv_rotary(const void* x, const void* w_qkv, int64_t m, int64_t k, i
   q.n_heads_kv = (int)n_heads_kv;
   q.head_dim = (int)head_dim;
   q.seqlen = (int)seqlen;
+  q.seq_offsets = nullptr;
+  q.slots = nullptr;
+  q.n_prompts = (int)(m / seqlen);
+  q.cache_rows = INT64_MAX;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == HX_BF16)
+    return gemm_half<__nv_bfloat16, HX_EPI_QKV_ROTARY>(x, w_qkv, nullptr, m, n, k, ldx, k, 0,
+                                                       nullptr, 0, workspace, workspace_bytes,
+                                                       dtype, s, &q);
+  return gemm_half<__half, HX_EPI_QKV_ROTARY>(x, w_qkv, nullptr, m, n, k, ldx, k, 0, nullptr, 0,
+                                              workspace, workspace_bytes, dtype, s, &q);
+}
+
+int hx_gemm_qkv_rotary_varlen(const void* x, const void* w_qkv, int64_t m, int64_t k,
+                              int64_t ldx, const int32_t* seq_offsets, const int32_t* slots,
+                              const int32_t* pos_start, int64_t n_prompts, int64_t n_heads,
+                              int64_t n_heads_kv, int64_t head_dim, const void* cos_table,
+                              const void* sin_table, int64_t table_rows, void* q_out, void* cache,
+                              int64_t cache_batch_stride, int64_t cache_seq_stride,
+                              int64_t cache_rows, int64_t cache_max_seq, void* workspace,
+                              size_t workspace_bytes, int dtype, void* stream) {
+  HX_REQUIRE(x && w_qkv && seq_offsets && slots && pos_start && cos_table && sin_table &&
+                 q_out && cache,
+             "hx_gemm_qkv_rotary_varlen: null pointer");
+  HX_REQUIRE(dtype == HX_BF16 || dtype == HX_F16, "hx_gemm_qkv_rotary_varlen: f16/bf16 only");
+  HX_REQUIRE(head_dim % 2 == 0 && n_heads > 0 && n_heads_kv > 0 && n_prompts > 0 &&
+                 n_prompts <= m && m <= INT32_MAX && cache_rows > 0,
+             "hx_gemm_qkv_rotary_varlen: bad shape");
+  HX_REQUIRE(cache_seq_stride >= 2 * n_heads_kv * head_dim && cache_seq_stride % 8 == 0 &&
+                 cache_batch_stride % 8 == 0 && (uintptr_t)cache % 16 == 0 &&
+                 (uintptr_t)q_out % 16 == 0 && (uintptr_t)cos_table % 16 == 0 &&
+                 (uintptr_t)sin_table % 16 == 0,
+             "hx_gemm_qkv_rotary_varlen: cache/q_out/tables must be 16-byte aligned (strides "
+             "multiples of 8)");
+  HX_REQUIRE((uintptr_t)x % 16 == 0 && (uintptr_t)w_qkv % 16 == 0 && ldx % 8 == 0 && k % 8 == 0,
+             "hx_gemm_qkv_rotary_varlen: x/w must be 16-byte aligned with ldx, k multiples of 8");
+  const int64_t n = (n_heads + 2 * n_heads_kv) * head_dim;
+  QkvArgs q;
+  q.q_out = q_out;
+  q.cache = cache;
+  q.cbs = cache_batch_stride;
+  q.css = cache_seq_stride;
+  q.cbo = 0;
+  q.max_seq = cache_max_seq;
+  q.table_rows = table_rows;
+  q.pos_start = pos_start;
+  q.cos = cos_table;
+  q.sin = sin_table;
+  q.n_heads = (int)n_heads;
+  q.n_heads_kv = (int)n_heads_kv;
+  q.head_dim = (int)head_dim;
+  q.seqlen = 1;
+  q.seq_offsets = seq_offsets;
+  q.slots = slots;
+  q.n_prompts = (int)n_prompts;
+  q.cache_rows = cache_rows;
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == HX_BF16)
     return gemm_half<__nv_bfloat16, HX_EPI_QKV_ROTARY>(x, w_qkv, nullptr, m, n, k, ldx, k, 0,

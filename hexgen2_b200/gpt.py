@@ -406,10 +406,10 @@ class GPTLMHeadModel(nn.Module):
         flat int64 CUDA tensor of sum(lengths) tokens, prompt i of lengths[i] tokens goes to
         batch row slots[i] of `caches` ({layer: [B, capacity, 2, hkv, d]}, positions 0..L-1).
         Every projection, norm and residual add runs once over all rows (GEMM M = sum of the
-        prompt lengths, which fills the GPU where a single prompt's rows do not); Wqkv runs as a
-        plain GEMM and each prompt's rotary + cache write and causal attention run on its own
-        row slice. Equals forward() of each prompt alone, logit for logit up to the summation
-        order of the projections. Returns the greedy next token of every prompt (int64 [n]; TP:
+        prompt lengths, which fills the GPU where a single prompt's rows do not); the Wqkv GEMM's
+        epilogue rotates and writes every prompt's rows to its own cache row, and the causal
+        attention of all prompts runs in one launch. Equals forward() of each prompt alone,
+        logit for logit up to the summation order of the projections. Returns the greedy next token of every prompt (int64 [n]; TP:
         one all-reduce of keys, as next_tokens) or, with greedy=False, the last-token logits
         [n, vocab] (gathered across TP ranks)."""
         n = len(lengths)
@@ -444,12 +444,18 @@ class GPTLMHeadModel(nn.Module):
         for i, layer in enumerate(layers):
             mixer, mlp = layer.mixer, layer.mlp
             cache = caches[i]
-            qkv = ops.gemm(normed, mixer.Wqkv.weight)
-            for b in range(n):
-                o, L = offs[b], lengths[b]
-                ops.rotary_cache_write(qkv[o:o + L], 1, L, hq, hk, d, zero, cos, sin, cache,
-                                       q_out=q[o:o + L].view(1, L, hq, d), batch_offset=slots[b],
-                                       interleaved=mixer.rotary_emb_interleaved)
+            if dtype != torch.float32 and mixer.rotary_emb_interleaved:
+                # Rotary + KV-cache write of every prompt in the Wqkv GEMM's epilogue.
+                ops.gemm_qkv_rotary_varlen(normed, mixer.Wqkv.weight, lengths, slots, hq, hk, d,
+                                           cos, sin, cache, q, meta=meta)
+            else:
+                qkv = ops.gemm(normed, mixer.Wqkv.weight)
+                for b in range(n):
+                    o, L = offs[b], lengths[b]
+                    ops.rotary_cache_write(qkv[o:o + L], 1, L, hq, hk, d, zero, cos, sin, cache,
+                                           q_out=q[o:o + L].view(1, L, hq, d),
+                                           batch_offset=slots[b],
+                                           interleaved=mixer.rotary_emb_interleaved)
             # All prompts' causal attention in one launch (one grid over heads x 128-query
             # blocks of every prompt); prompt by prompt where that kernel does not apply.
             if not ops.prefill_attention_varlen(q, cache, lengths, slots, hk, self.scale, ctx,

@@ -168,6 +168,30 @@ def gemm_qkv_rotary(x, w_qkv, seqlen, n_heads, n_heads_kv, head_dim, pos_start, 
     return q_out
 
 
+def gemm_qkv_rotary_varlen(x, w_qkv, lengths, slots, n_heads, n_heads_kv, head_dim, cos, sin,
+                           cache, q_out, meta=None):
+    """gemm_qkv_rotary over prompts packed row after row in x [T, K] (prompt b: lengths[b]
+    rows, cache row slots[b], positions from 0): q into q_out [T, n_heads, head_dim], k and v
+    into cache[slots[b], s]. meta: a varlen_meta table (the same one prefill_attention_varlen
+    reads; built here when omitted)."""
+    _require_cuda(x, w_qkv, cache, q_out)
+    M, K = x.shape
+    N = w_qkv.shape[0]
+    n = len(lengths)
+    table, _, _ = meta if meta is not None else varlen_meta(lengths, slots, x.device)
+    base = table.data_ptr()
+    code = _code(x)
+    nbytes = _L().hx_gemm_workspace(M, N, K, _lib.HX_EPI_QKV_ROTARY, code)
+    ws = workspace(nbytes, kind="gemm")
+    check(_L().hx_gemm_qkv_rotary_varlen(
+        _p(x), _p(w_qkv), M, K, x.stride(0), base, base + 4 * (n + 1), base + 4 * (2 * n + 1), n,
+        n_heads, n_heads_kv, head_dim, _p(cos), _p(sin), cos.shape[0], _p(q_out), _p(cache),
+        cache.stride(0), cache.stride(1), cache.shape[0], cache.shape[1], _p(ws), nbytes, code,
+        _stream()), "hx_gemm_qkv_rotary_varlen")
+    _count(2 if (nbytes and M > 64) else 1)
+    return q_out
+
+
 def gemm_workspace_bytes(M, N, K, epilogue, dtype) -> int:
     return _L().hx_gemm_workspace(M, N, K, epilogue, DTYPE_CODE[dtype])
 

@@ -138,6 +138,23 @@ int hx_gemm_qkv_rotary(const void* x, const void* w_qkv, int64_t m, int64_t k, i
                        int64_t cache_max_seq, void* workspace, size_t workspace_bytes, int dtype,
                        void* stream);
 
+/* hx_gemm_qkv_rotary over prompts of different lengths packed row after row: prompt b owns
+ * rows [seq_offsets[b], seq_offsets[b+1]) of x (n_prompts + 1 offsets, seq_offsets[0] = 0,
+ * the last = m), and row seq_offsets[b] + s is rotated at position pos_start[b] + s and its k, v
+ * go to cache[slots[b], pos] (0 <= slots[b] < cache_rows). seq_offsets, slots and pos_start are
+ * device int32 arrays. A row whose slot or position falls outside the cache is never written and
+ * sets the device error word to 2 (bad argument; see hx_device_error); the call's other outputs
+ * are then unspecified, since waits that see the error word stop early. Replaces the per-prompt mha.py:542 + :557 + :286 of a
+ * packed prefill pass in one launch. */
+int hx_gemm_qkv_rotary_varlen(const void* x, const void* w_qkv, int64_t m, int64_t k,
+                              int64_t ldx, const int32_t* seq_offsets, const int32_t* slots,
+                              const int32_t* pos_start, int64_t n_prompts, int64_t n_heads,
+                              int64_t n_heads_kv, int64_t head_dim, const void* cos_table,
+                              const void* sin_table, int64_t table_rows, void* q_out, void* cache,
+                              int64_t cache_batch_stride, int64_t cache_seq_stride,
+                              int64_t cache_rows, int64_t cache_max_seq, void* workspace,
+                              size_t workspace_bytes, int dtype, void* stream);
+
 /* ---------------------------------------------------------------- attention */
 /* Multi-query (prefill) attention over the KV cache written by hx_rotary_cache_write.
  * q: [batch, seqlen_q, n_heads, head_dim]; keys/values are cache[cache_batch_offset + b,

@@ -454,6 +454,52 @@ def test_decode_gemm_is_deterministic_and_needs_no_workspace(ops, M, N, K):
 
 
 # ------------------------------------------------------------------------------ varlen prefill
+@pytest.mark.parametrize("lens,hq,hk,d", [([1, 17, 30], 8, 2, 128),          # M <= 64: decode kernel
+                                          ([129, 1, 70], 8, 2, 128),         # split-K tcgen05 tiles
+                                          ([5, 300, 77], 16, 2, 64),
+                                          ([700, 1300, 1, 64], 32, 8, 128)])  # CTA-pair tiles
+def test_gemm_qkv_rotary_varlen_matches_per_prompt(ops, lens, hq, hk, d):
+    """Packed prompts through the Wqkv GEMM with rotary + cache write in its epilogue (each
+    row rotated at its position within its prompt, k/v into the prompt's cache slot) == the
+    plain GEMM followed by hx_rotary_cache_write prompt by prompt (within one bf16 ulp:
+    the two kernels may contract the rotary's multiply-adds differently); slots not named stay
+    untouched. A slot outside the cache is never written and is reported in the device
+    error word."""
+    dt, h = torch.bfloat16, hq * d
+    n = len(lens)
+    slots = [(3 * i + 1) % (n + 1) for i in range(n)]
+    T, cap = sum(lens), max(lens) + 3
+    g = torch.Generator().manual_seed(T + hq)
+    x = torch.randn(T, h, generator=g).to(dt).cuda()
+    w = (torch.randn((hq + 2 * hk) * d, h, generator=g) * 0.05).to(dt).cuda()
+    cos, sin = Rotary(d, 10000.0).tables(cap, dt)
+    cos, sin = cos.cuda(), sin.cuda()
+    c_ref = torch.zeros(n + 1, cap, 2, hk, d, dtype=dt, device="cuda")
+    c_new = torch.zeros_like(c_ref)
+    qkv = ops.gemm(x, w)
+    zero = torch.zeros(1, dtype=torch.int32, device="cuda")
+    q_ref = torch.empty(T, hq, d, dtype=dt, device="cuda")
+    o = 0
+    for b, L in enumerate(lens):
+        ops.rotary_cache_write(qkv[o:o + L], 1, L, hq, hk, d, zero, cos, sin, c_ref,
+                               q_out=q_ref[o:o + L].view(1, L, hq, d), batch_offset=slots[b])
+        o += L
+    q_new = torch.full_like(q_ref, float("nan"))
+    ops.gemm_qkv_rotary_varlen(x, w, lens, slots, hq, hk, d, cos, sin, c_new, q_new)
+    assert ops.device_error() == 0
+    torch.testing.assert_close(q_new.float(), q_ref.float(), rtol=2 ** -7, atol=1e-6)
+    torch.testing.assert_close(c_new.float(), c_ref.float(), rtol=2 ** -7, atol=1e-6)
+    unused = sorted(set(range(n + 1)) - set(slots))
+    assert all(not c_new[u].any() for u in unused)
+    # Slot n + 1 lies past the cache view's n + 1 rows: the guard row behind the view stays
+    # untouched and the call reports a bad argument (its other outputs are then unspecified).
+    guarded = torch.zeros(n + 2, cap, 2, hk, d, dtype=dt, device="cuda")
+    ops.gemm_qkv_rotary_varlen(x, w, lens, [n + 1] + slots[1:], hq, hk, d, cos, sin,
+                               guarded[:n + 1], torch.empty_like(q_ref))
+    assert ops.device_error() == 2
+    assert not guarded[n + 1].any()
+
+
 @pytest.mark.parametrize("hq,hk,d", [(32, 32, 128), (32, 8, 128), (16, 2, 64)])
 def test_prefill_attention_varlen_equals_per_prompt(ops, hq, hk, d):
     """Ragged prompts packed row after row (lengths 1, 127, 128, 129, 300, 700; permuted cache
