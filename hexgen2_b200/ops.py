@@ -212,11 +212,14 @@ def prefill_attention(q, cache, pos_start, n_heads_kv, softmax_scale, causal=Tru
     return out
 
 
-def varlen_meta(lengths, slots, device):
-    """Device table for prefill_attention_varlen: row offsets [n + 1], cache slots [n], start
-    positions [n] (0: prefill from an empty cache) and the (prompt, 128-query block) work items,
-    heaviest causal work (latest block) first. Returns (table, n_items, items start index)."""
+def varlen_table(lengths, slots):
+    """Host layout of a packed pass's metadata, as int32 values: row offsets [n + 1], cache
+    slots [n], start positions [n] (0: prefill from an empty cache), a pad to an even count, then
+    the (prompt, 128-query block) work items, heaviest causal work (latest block) first.
+    Returns (values, n_items, index of the first item)."""
     n = len(lengths)
+    if n == 0 or len(slots) != n or any(L <= 0 for L in lengths):
+        raise ValueError("varlen_table needs one slot and a positive length per prompt")
     offs = [0]
     for L in lengths:
         offs.append(offs[-1] + L)
@@ -225,8 +228,16 @@ def varlen_meta(lengths, slots, device):
     head = offs + list(slots) + [0] * n
     if len(head) % 2:
         head.append(0)  # the (prompt, block) pairs are read as 8-byte int2
-    meta = torch.tensor(head + [v for it in items for v in it], dtype=torch.int32).pin_memory()
-    return meta.to(device, non_blocking=True), len(items), len(head)
+    return head + [v for it in items for v in it], len(items), len(head)
+
+
+def varlen_meta(lengths, slots, device):
+    """varlen_table on the device (pinned host copy, asynchronous H2D on the current stream):
+    the table prefill_attention_varlen and gemm_qkv_rotary_varlen read. Returns (table,
+    n_items, items start index)."""
+    values, n_items, items_at = varlen_table(lengths, slots)
+    meta = torch.tensor(values, dtype=torch.int32).pin_memory()
+    return meta.to(device, non_blocking=True), n_items, items_at
 
 
 def prefill_attention_varlen(q, cache, lengths, slots, n_heads_kv, softmax_scale, out,
