@@ -191,7 +191,10 @@ class KVHandoff:
     mapped peer address as its destination, so the live rows of all layers cross NVLink inside
     one kernel with no staging copy and no per-layer messages. The control message (an int64
     tensor) is sent through the process group only after the kernel has completed, so the
-    receiver never reads a partially written buffer.
+    receiver never reads a partially written buffer. Nothing here stops a second pack from
+    overwriting bytes the receiver has not consumed yet: a sender that reuses the buffer waits
+    for the receiver's release first (the serving loop reserves regions of a ring and frees
+    them on the decode rank's release message, serving.ByteRing).
     """
 
     def __init__(self, peer: int, group=None):
