@@ -18,12 +18,14 @@ engine touches; both shims live here, outside the reference tree:
     :99-101, :112): prefill and decode are the engine's steps with the cache read from and
     written to DynamicCache layers.
 
-The checkpoint has Llama-2-7B widths and seeded random weights; it is written to a temporary
-directory under oracle/_ref/ (git-ignored) and removed at exit. Each engine is timed at 1 and
-`--depth` decoder layers (medians of three) and the per-layer cost is extrapolated to 32 layers,
-as the bench's CPU arm does.
+Configs: `llama7b` (config 3 widths, bf16, batch 1; timed at 1 and `--depth`
+decoder layers and extrapolated to 32, as the bench's CPU arm does), `tinyllama` (config 2,
+all 22 layers, bf16, a 512-token prompt and 128 new tokens) and `fixture` (config 1, the seeded
+2-layer fixture in f32, prompts of 8-32 tokens, 16 new tokens). Checkpoints have seeded random
+weights and are written to a temporary directory under oracle/_ref/ (git-ignored), removed at
+exit. Every figure is the median of three runs.
 
-  python tests/cpu_reference_timing.py --reference <HexGen-2 checkout> [--prompts 285,750]
+  python tests/cpu_reference_timing.py --reference <HexGen-2 checkout> [--config llama7b]
 """
 from __future__ import annotations
 
@@ -48,6 +50,14 @@ WIDTHS = dict(vocab_size=32000, hidden_size=4096, intermediate_size=11008,
               num_attention_heads=32, num_key_value_heads=32, max_position_embeddings=4096,
               rms_norm_eps=1e-5, rope_theta=10000.0, bos_token_id=1, eos_token_id=2,
               tie_word_embeddings=False)
+TINYLLAMA = dict(vocab_size=32000, hidden_size=2048, intermediate_size=5632,
+                 num_attention_heads=32, num_key_value_heads=4, max_position_embeddings=2048,
+                 rms_norm_eps=1e-5, rope_theta=10000.0, bos_token_id=1, eos_token_id=2,
+                 tie_word_embeddings=False)
+# name: (widths or None for the fixture, full depth, dtype, default prompts, new tokens, fit)
+CONFIGS = {"llama7b": (WIDTHS, 32, "bfloat16", "285,750", 16, True),
+           "tinyllama": (TINYLLAMA, 22, "bfloat16", "512", 128, False),
+           "fixture": (None, 2, "float32", "8,16,32", 16, False)}
 
 
 def reference_engine(ref_root: Path):
@@ -103,11 +113,15 @@ def reference_engine(ref_root: Path):
     return ShimmedEngine
 
 
-def write_checkpoint(folder: Path, layers: int, seed: int):
+def write_checkpoint(folder: Path, widths, layers: int, dtype, seed: int):
+    if widths is None:  # the seeded correctness fixture (config 1)
+        from hexgen2_b200.fixture import create
+        create(folder, seed=17)
+        return
     from transformers import LlamaConfig, LlamaForCausalLM
     torch.manual_seed(seed)
-    cfg = LlamaConfig(num_hidden_layers=layers, **WIDTHS)
-    model = LlamaForCausalLM(cfg).to(torch.bfloat16)
+    cfg = LlamaConfig(num_hidden_layers=layers, **widths)
+    model = LlamaForCausalLM(cfg).to(dtype)
     model.save_pretrained(str(folder), safe_serialization=True)
     del model
 
@@ -148,54 +162,69 @@ def host_info():
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True, help="HexGen-2 checkout (hexgen2/ inside)")
-    ap.add_argument("--prompts", default="285,750", help="prompt lengths (the bench's first two)")
-    ap.add_argument("--new-tokens", type=int, default=8)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="llama7b")
+    ap.add_argument("--prompts", default=None, help="prompt lengths (default per config)")
+    ap.add_argument("--new-tokens", type=int, default=None)
     ap.add_argument("--threads", default="1,all")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--depth", type=int, default=8, help="second depth of the per-layer fit")
     args = ap.parse_args()
+    widths, full, dname, dprompts, dnew, fit = CONFIGS[args.config]
+    dtype = getattr(torch, dname)
+    new_tokens = args.new_tokens or dnew
     Engine = reference_engine(Path(args.reference))
-    lens = [int(x) for x in args.prompts.split(",")]
+    lens = [int(x) for x in (args.prompts or dprompts).split(",")]
+    vocab = widths["vocab_size"] if widths else 128
     g = torch.Generator().manual_seed(args.seed + 1)
-    prompts = [torch.randint(3, 32000, (L,), generator=g).tolist() for L in lens]
+    prompts = [torch.randint(3, vocab, (L,), generator=g).tolist() for L in lens]
     threads = [os.cpu_count() if t == "all" else int(t) for t in args.threads.split(",")]
-    out = {"host": host_info(), "dtype": "bf16", "prompts": lens, "new_tokens": args.new_tokens,
-           "widths": "Llama-2-7B", "runs": {}}
+    depths = (1, args.depth) if fit else (full,)
+    out = {"host": host_info(), "config": args.config, "dtype": dname, "prompts": lens,
+           "new_tokens": new_tokens, "layers": full, "measured_depths": list(depths), "runs": {}}
     scratch = ROOT / "oracle" / "_ref"
     scratch.mkdir(parents=True, exist_ok=True)
     with tempfile.TemporaryDirectory(dir=scratch) as tmp:
         raw = {}
-        for layers in (1, args.depth):
+        for layers in depths:
             folder = Path(tmp) / f"L{layers}"
-            write_checkpoint(folder, layers, args.seed)
+            write_checkpoint(folder, widths, layers, dtype, args.seed)
             for nt in threads:
                 torch.set_num_threads(nt)
-                ref = Engine(str(folder), engine="hf-reference", device="cpu", dtype="bfloat16")
-                r_pre, r_dec, r_tok = time_engine(ref, prompts, args.new_tokens)
+                ref = Engine(str(folder), engine="hf-reference", device="cpu", dtype=dname)
+                r_pre, r_dec, r_tok = time_engine(ref, prompts, new_tokens)
                 del ref
-                shape, state = load_hf_checkpoint(folder, dtype=torch.bfloat16)
-                port = OracleModel(shape, state, dtype=torch.bfloat16)
-                p_pre, p_dec, p_tok = time_engine(port, prompts, args.new_tokens)
+                shape, state = load_hf_checkpoint(folder, dtype=dtype)
+                port = OracleModel(shape, state, dtype=dtype)
+                p_pre, p_dec, p_tok = time_engine(port, prompts, new_tokens)
                 del port, state
                 raw[(layers, nt)] = {"reference": (r_pre, r_dec), "port": (p_pre, p_dec),
                                      "tokens_agree": sum(a == b for a, b in zip(r_tok, p_tok))}
                 print(layers, nt, raw[(layers, nt)], flush=True)
-    D = args.depth
     for nt in threads:
         row = {}
         for kind in ("reference", "port"):
-            (pre1, dec1), (pre2, dec2) = raw[(1, nt)][kind], raw[(D, nt)][kind]
-            pre32 = [a + 31 * (b - a) / (D - 1) for a, b in zip(pre1, pre2)]  # t(1) + 31 x per-layer
-            dec32 = dec1 + 31 * (dec2 - dec1) / (D - 1)
-            row[kind] = {"prefill_ms_32_layers": [round(x, 1) for x in pre32],
-                         "decode_ms_per_token_32_layers": round(dec32, 1),
-                         f"prefill_ms_measured_1_{D}_layers": [[round(x, 1) for x in pre1], [round(x, 1) for x in pre2]],
+            if fit:
+                D = args.depth
+                (pre1, dec1), (pre2, dec2) = raw[(1, nt)][kind], raw[(D, nt)][kind]
+                # t(1) + (full - 1) x per-layer
+                pre = [a + (full - 1) * (b - a) / (D - 1) for a, b in zip(pre1, pre2)]
+                dec = dec1 + (full - 1) * (dec2 - dec1) / (D - 1)
+                extra = {f"prefill_ms_measured_1_{D}_layers": [[round(x, 1) for x in pre1],
+                                                               [round(x, 1) for x in pre2]],
                          f"decode_ms_measured_1_{D}_layers": [round(dec1, 2), round(dec2, 2)]}
-        row["port_over_reference_decode"] = round(row["reference"]["decode_ms_per_token_32_layers"]
-                                                  / row["port"]["decode_ms_per_token_32_layers"], 3)
-        row["port_over_reference_prefill"] = round(sum(row["reference"]["prefill_ms_32_layers"])
-                                                   / sum(row["port"]["prefill_ms_32_layers"]), 3)
-        row["greedy_tokens_agree"] = [raw[(L, nt)]["tokens_agree"] for L in (1, D)]
+            else:
+                pre, dec = raw[(full, nt)][kind]
+                extra = {}
+            # One request of the first prompt's length: new_tokens / (prefill + decode).
+            tps = new_tokens / ((pre[0] + (new_tokens - 1) * dec) / 1e3)
+            row[kind] = {f"prefill_ms_{full}_layers": [round(x, 2) for x in pre],
+                         f"decode_ms_per_token_{full}_layers": round(dec, 2),
+                         "tokens_per_s_first_prompt": round(tps, 3), **extra}
+        row["port_over_reference_decode"] = round(row["reference"][f"decode_ms_per_token_{full}_layers"]
+                                                  / row["port"][f"decode_ms_per_token_{full}_layers"], 3)
+        row["port_over_reference_prefill"] = round(sum(row["reference"][f"prefill_ms_{full}_layers"])
+                                                   / sum(row["port"][f"prefill_ms_{full}_layers"]), 3)
+        row["greedy_tokens_agree"] = [raw[(L, nt)]["tokens_agree"] for L in depths]
         out["runs"][str(nt)] = row
     print(json.dumps(out))
 
