@@ -54,9 +54,21 @@ class Engine:
         if self.config.model_type != "llama" or (
                 scaling is not None and scaling.get("rope_type", "default") != "default"):
             raise ValueError("This baseline supports Llama architecture without RoPE scaling")
+        if engine == "hf-reference":
+            # The reference's validation engine (hexgen2/model.py:32-37): transformers' eager
+            # LlamaForCausalLM on any device, chosen explicitly by the caller. It runs none of
+            # this package's kernels, and the native engine never falls back to it.
+            from transformers import LlamaForCausalLM
+            self.kind = engine
+            self.model = LlamaForCausalLM.from_pretrained(
+                model_dir, local_files_only=True, dtype=self.dtype, use_safetensors=True,
+                attn_implementation="eager").to(self.device).eval()
+            c = self.config
+            self.num_layers, self.kv_heads = c.num_hidden_layers, c.num_key_value_heads
+            self.head_dim = c.hidden_size // c.num_attention_heads
+            return
         if engine != "native":
-            raise ValueError("hexgen2_b200 provides the native engine only; hf-reference is the "
-                             "reference's CPU validation backend")
+            raise ValueError(f"unknown engine {engine!r}: 'native' or 'hf-reference'")
         self.kind = engine
         _check_device(self.device)
         if self.device.index is not None:
@@ -108,8 +120,14 @@ class Engine:
         self.row_bytes = 2 * m.hk * m.head_dim * torch.empty((), dtype=self.dtype).element_size()
 
     # ------------------------------------------------------------------ prefill / decode
+    def _native_only(self, what: str):
+        if self.kind != "native":
+            raise ValueError(f"{what} needs the native engine (this one is {self.kind!r})")
+
     @torch.inference_mode()
     def prefill(self, input_ids, max_new_tokens):
+        if self.kind == "hf-reference":
+            return self._hf_prefill(input_ids)
         ids = torch.tensor([input_ids], dtype=torch.long, device=self.device)
         L = len(input_ids)
         state = CacheState(L + max_new_tokens)
@@ -122,6 +140,7 @@ class Engine:
     def pack_live(self, caches: dict, lengths: list[int], batch_rows=None):
         """Gathers rows [0, L_b) of cache slot b of every layer into one buffer per request.
         Returns a list (one per request) of {layer: [1, L_b, 2, hkv, d]} contiguous views."""
+        self._native_only("pack_live")
         n = self.num_layers
         big0 = caches[0]
         layer_stride = (caches[1].data_ptr() - big0.data_ptr()) if n > 1 else 0
@@ -176,18 +195,35 @@ class Engine:
                       big.stride(2) * elem, self.row_bytes, max(lengths))
         return {i: big[i] for i in range(n)}
 
-    @torch.inference_mode()
-    def decode(self, first_token, cache, prompt_length, max_new_tokens, on_token=None):
-        token = first_token.to(self.device).reshape(1)
-        generated = [int(token.item())]
-        if on_token:
-            on_token(generated[-1])
+    def _hf_prefill(self, input_ids):
+        """hexgen2/model.py:73-78 for the hf-reference engine; transformers' DynamicCache
+        replaces the tuple cache the reference reads (its layers hold [1, hkv, L, d] keys and
+        values), and the cache goes out as {layer: [1, L, 2, hkv, d]} as there."""
+        ids = torch.tensor([input_ids], dtype=torch.long, device=self.device)
+        result = self.model(ids, use_cache=True)
+        cache = {i: torch.stack((l.keys.transpose(1, 2), l.values.transpose(1, 2)), dim=2).contiguous()
+                 for i, l in enumerate(result.past_key_values.layers)}
+        logits = result.logits[:, -1]
+        return logits.argmax(-1), cache, logits
+
+    def _check_live_cache(self, cache, prompt_length):
+        """hexgen2/model.py:90-97."""
         if set(cache) != set(range(self.config.num_hidden_layers)):
             raise ValueError("KV cache does not match the configured layer count")
         expected = (1, prompt_length, 2, self.kv_heads, self.head_dim)
         for value in cache.values():
             if tuple(value.shape) != expected or value.dtype != self.dtype:
                 raise ValueError("KV cache shape/dtype does not match checkpoint and prompt")
+
+    @torch.inference_mode()
+    def decode(self, first_token, cache, prompt_length, max_new_tokens, on_token=None):
+        token = first_token.to(self.device).reshape(1)
+        generated = [int(token.item())]
+        if on_token:
+            on_token(generated[-1])
+        self._check_live_cache(cache, prompt_length)
+        if self.kind == "hf-reference":
+            return self._hf_decode(token, cache, max_new_tokens, generated, on_token)
         state = CacheState(prompt_length + max_new_tokens)
         state.sequence_len_offset = prompt_length
         state.key_value_memory_dict = self.unpack_live([dict(cache)], [prompt_length],
@@ -196,6 +232,25 @@ class Engine:
             logits = self.model(token[:, None], inference_params=state, last_token_only=True).logits
             state.sequence_len_offset += 1
             token = ops.argmax(logits)
+            generated.append(int(token.item()))
+            if on_token:
+                on_token(generated[-1])
+        return generated
+
+    def _hf_decode(self, token, cache, max_new_tokens, generated, on_token):
+        """hexgen2/model.py:98-121 for the hf-reference engine, the live cache handed to
+        transformers as a DynamicCache."""
+        from transformers import DynamicCache
+
+        past = DynamicCache()
+        for i in range(len(cache)):
+            kv = cache[i].to(self.device)
+            past.update(kv[:, :, 0].transpose(1, 2).contiguous(),
+                        kv[:, :, 1].transpose(1, 2).contiguous(), i)
+        for _ in range(max_new_tokens - 1):
+            result = self.model(token[:, None], past_key_values=past, use_cache=True)
+            past, logits = result.past_key_values, result.logits[:, -1]
+            token = logits.argmax(-1)
             generated.append(int(token.item()))
             if on_token:
                 on_token(generated[-1])
@@ -217,6 +272,7 @@ class Engine:
         buffer) and captures. With capture_first (for callers that already ran a step on these
         buffers, so every scratch buffer is sized), a missing graph is captured at the first
         step instead, so even single-step calls replay."""
+        self._native_only("decode_batch")
         B = first_tokens.numel()
         capacity = caches[0].shape[1]
         tokens = torch.empty(steps + 1, B, dtype=torch.long, device=self.device)
@@ -277,6 +333,7 @@ class Engine:
         `cache`) in packed passes of at most max_tokens tokens / max_prompts prompts
         (GPTLMHeadModel.prefill_packed), writing each greedy first token into first[b]. With
         events, events[b] is recorded when prompt b's first token is ready."""
+        self._native_only("prefill_chunks")
         offs = [0]
         for L in lengths:
             offs.append(offs[-1] + L)
@@ -300,6 +357,7 @@ class Engine:
         prompts are prefilled in packed passes straight into their slots of one all-layer
         cache, then the whole ragged batch decodes together. Returns a list of max_new_tokens
         tokens per request."""
+        self._native_only("serve_batch")
         if isinstance(prompts, torch.Tensor):
             flat, lens = prompts, list(lengths)
         else:
@@ -334,6 +392,7 @@ class ContinuousBatcher:
     """
 
     def __init__(self, engine: Engine, slots: int, capacity: int):
+        engine._native_only("ContinuousBatcher")
         self.eng, self.slots, self.capacity = engine, slots, capacity
         dev = engine.device
         self.cache = engine.model.allocate_inference_cache(slots, capacity)

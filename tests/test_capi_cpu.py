@@ -64,14 +64,16 @@ def test_ops_refuse_cpu_tensors():
         ops.rmsnorm(torch.zeros(2, 8), torch.ones(8), 1e-6)
 
 
-def test_engine_refuses_cpu(tmp_path):
+def test_native_engine_refuses_cpu(tmp_path):
+    """The native engine has no CPU path (the explicitly chosen hf-reference engine is
+    transformers' own model, tests/test_engine_hf_cpu.py)."""
     from hexgen2_b200 import Engine
     from hexgen2_b200.fixture import create
     folder = create(tmp_path / "m", seed=0)
     with pytest.raises(ValueError):
         Engine(folder, device="cpu", dtype="float32")
     with pytest.raises(ValueError):
-        Engine(folder, engine="hf-reference", device="cpu", dtype="float32")
+        Engine(folder, engine="native", device="cpu", dtype="float32")
 
 
 def test_graft_build_compiles_for_sm100a():
