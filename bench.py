@@ -122,10 +122,11 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------
 # Native arm, N = 1 (colocated)
 # ------------------------------------------------------------------------------------------
-# DRAM bytes per algorithmic byte of each decode-step kernel class, from the ncu capture
-# summarised in profiles/decode_step_dram_llama7b_b32.md (dram__bytes_read.sum +
-# dram__bytes_write.sum over one decode step's launches of the class / the algorithmic bytes of
-# those launches). bench.py cannot run ncu; it scales its own algorithmic bytes by these.
+# DRAM bytes per algorithmic byte of each decode-step kernel class, from one ncu capture of this
+# bench with 2 of the 32 layers (dram__bytes_read.sum + dram__bytes_write.sum over one decode
+# step's launches of the class / the algorithmic bytes of those launches; the summary is kept
+# with the other ncu summaries). bench.py cannot run ncu; it scales its own algorithmic bytes
+# by these.
 DRAM_PER_ALGORITHMIC = {"gemm_decode": 0.996, "decode_attention": 1.017, "rmsnorm": 0.418}
 DRAM_SOURCE = "profiles/decode_step_dram_llama7b_b32.md (ncu dram__bytes_read/write, scaled)"
 

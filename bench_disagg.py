@@ -28,7 +28,7 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-NVLINK_PEER_GBS = 778.0     # measured peer copy per direction (profiles/nvlink_peer_copy.md)
+NVLINK_PEER_GBS = 778.0     # measured peer copy per direction, one GPU pair (`--workload peer_copy`)
 NVLINK_NOMINAL_GBS = 900.0  # NVLink 5 per direction per GPU
 
 LLAMA2_70B = dict(vocab_size=32000, hidden_size=8192, intermediate_size=28672,
