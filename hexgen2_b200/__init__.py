@@ -5,7 +5,9 @@ Public API (mirrors the reference's):
     GPTLMHeadModel, InferenceParams        hexgen/hexgen_core/models/gpt.py
     send_packet, recv_packet, send_data,
     recv_data, validate_header, KVHandoff  hexgen2/transport.py (+ the NVLink direct path)
-The compute runs in libhexgen2_b200.so (see include/hexgen2_b200.h); there is no CPU path.
+The native engine's compute runs in libhexgen2_b200.so (see include/hexgen2_b200.h) and has
+no CPU path; Engine(engine="hf-reference") is the reference's transformers-eager validation
+engine, chosen explicitly, and runs none of it.
 """
 from .engine import ContinuousBatcher, Engine, serve_arrivals
 from .gpt import CacheState, GPTLMHeadModel, InferenceParams

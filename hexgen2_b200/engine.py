@@ -13,7 +13,8 @@ and the same ValueError conditions. Differences that do not change results:
   * greedy argmax runs on the GPU (hx_argmax, torch.argmax tie-breaking).
 Also: Engine.from_config(...) builds a seeded random-init model of any Llama shape on the
 device (no checkpoint files), and decode_batch() runs ragged batches with per-sequence
-lengths (continuous-batching building block).
+lengths (continuous-batching building block). Engine(..., engine="hf-reference") is the
+reference's validation engine (transformers' eager LlamaForCausalLM, prefill / decode only).
 """
 from __future__ import annotations
 
