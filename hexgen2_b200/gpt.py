@@ -68,6 +68,21 @@ def _pg_size(pg):
     return 1 if pg is None else dist.get_world_size(pg)
 
 
+def argmax_keys(values: torch.Tensor, global_index: torch.Tensor) -> torch.Tensor:
+    """int64 keys whose maximum over tensor-parallel ranks is the greedy token of the whole
+    vocabulary: the high 32 bits order the f32 values (sign-magnitude bits made monotone,
+    -0.0 folded into +0.0), the low 32 bits hold 2^32 - 1 - index, so equal values resolve to
+    the lowest vocabulary index, as torch.argmax over the gathered logits does."""
+    bits = (values.float() + 0.0).view(torch.int32)
+    ordered = torch.where(bits < 0, bits ^ 0x7FFFFFFF, bits).to(torch.int64)
+    return ordered * 4294967296 + (4294967295 - global_index.to(torch.int64))
+
+
+def key_index(key: torch.Tensor) -> torch.Tensor:
+    """Vocabulary index carried by an argmax_keys key."""
+    return 4294967295 - (key & 4294967295)
+
+
 def _pg_rank(pg):
     return 0 if pg is None else dist.get_rank(pg)
 
@@ -521,13 +536,10 @@ class GPTLMHeadModel(nn.Module):
     def _tp_argmax(self, local_logits, out=None):
         rows, vloc = local_logits.shape
         idx = ops.argmax(local_logits)
-        val = local_logits.gather(1, idx.view(rows, 1)).view(rows).float()
-        bits = val.view(torch.int32)
-        ordered = torch.where(bits < 0, bits ^ 0x7FFFFFFF, bits).to(torch.int64)
-        gidx = idx + _pg_rank(self.process_group) * vloc
-        key = ordered * 4294967296 + (4294967295 - gidx)
+        val = local_logits.gather(1, idx.view(rows, 1)).view(rows)
+        key = argmax_keys(val, idx + _pg_rank(self.process_group) * vloc)
         dist.all_reduce(key, op=dist.ReduceOp.MAX, group=self.process_group)
-        win = 4294967295 - (key & 4294967295)
+        win = key_index(key)
         if out is None:
             return win
         out.copy_(win)
