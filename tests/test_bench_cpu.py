@@ -39,3 +39,21 @@ def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"}, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_roofline_byte_counts_match_llama2_7b():
+    """The algorithmic bytes behind `roofline.achieved`: every Llama-2-7B weight once per decode
+    step (6.74 G linear parameters incl. the LM head = 13.48 GB in bf16) plus activations, and
+    the live K/V rows of every sequence in every layer."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    cfg = bench.LLAMA2_7B
+    assert bench.layer_params(cfg) == 202_375_168
+    weights = (32 * 202_375_168 + 32000 * 4096) * 2
+    b = bench.decode_step_bytes(cfg, [1000] * 32)
+    # Activations at batch 32 add about 1 % (inputs, outputs and residual reads of every GEMM).
+    assert weights < b["gemm_decode"] < weights * 1.015
+    assert b["gemm_decode"] == 13_353_828_352  # the figure the bench lines report
+    kv = 32 * (32 * 1000) * 2 * 32 * 128 * 2
+    assert kv < b["decode_attention"] < kv * 1.001
+    assert b["rmsnorm"] == (2 * 32 + 1) * (2 * 32 * 4096 * 2 + 4096 * 2)
