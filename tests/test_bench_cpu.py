@@ -54,6 +54,7 @@ def test_roofline_byte_counts_match_llama2_7b():
     # Activations at batch 32 add about 1 % (inputs, outputs and residual reads of every GEMM).
     assert weights < b["gemm_decode"] < weights * 1.015
     assert b["gemm_decode"] == 13_353_828_352  # the figure the bench lines report
-    kv = 32 * (32 * 1000) * 2 * 32 * 128 * 2
-    assert kv < b["decode_attention"] < kv * 1.001
+    kv = 32 * (32 * 1000) * 2 * 32 * 128 * 2        # layers x live rows x (K, V) x hkv x d x 2 B
+    q_out = 32 * 2 * 32 * 32 * 128 * 2               # layers x (q, out) x B x hq x d x 2 B
+    assert b["decode_attention"] == kv + q_out
     assert b["rmsnorm"] == (2 * 32 + 1) * (2 * 32 * 4096 * 2 + 4096 * 2)
