@@ -180,3 +180,20 @@ def test_remap_equals_reference_remap(tied, multiple):
     assert set(ours) == set(theirs)
     for k in theirs:
         assert torch.equal(ours[k], theirs[k]), k
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_random_init_gives_every_tp_layout_the_same_model(world):
+    """random_native_state with tp_world > 1 slices each seeded full tensor to the rank's shard,
+    so the TP ranks of a random-init model together hold exactly the TP-1 model (what the
+    multi-GPU serving runs rely on when they compare TP decode groups with a colocated run)."""
+    from hexgen2_b200.checkpoint import config_from_dict, random_native_state, shard_state_dict_tp
+    cfg = config_from_dict(dict(SMALL, num_key_value_heads=4, vocab_size=64))
+    full = random_native_state(cfg, seed=3, dtype=torch.float32, device="cpu")
+    for rank in range(world):
+        part = random_native_state(cfg, seed=3, dtype=torch.float32, device="cpu",
+                                   tp_world=world, tp_rank=rank)
+        want = shard_state_dict_tp(full, cfg, world, rank)
+        assert set(part) == set(want)
+        for k in want:
+            assert torch.equal(part[k], want[k]), (rank, k)
