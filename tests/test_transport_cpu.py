@@ -175,3 +175,23 @@ def test_interop_with_reference_transport(tmp_path):
     """This package's send_packet/send_data feed the reference's recv_packet/recv_data and the
     reverse (hexgen2/transport.py:44-100), on a real 2-process Gloo group."""
     mp.spawn(_interop_worker, args=(str(tmp_path / "rendezvous"),), nprocs=2, join=True)
+
+
+def test_cache_geometry_and_head_slice_bytes():
+    """The re-shard path's host checks: an engine cache is one all-layer tensor handed out as
+    per-layer views at a fixed stride, and a head slice's packed size is K + V slabs of every
+    layer; views not at one fixed stride and rows
+    that are not contiguous are rejected."""
+    from hexgen2_b200.transport import _cache_geometry, head_slice_bytes
+    layers, B, cap, hk, d = 3, 2, 16, 4, 8
+    big = torch.zeros(layers, B, cap, 2, hk, d, dtype=torch.bfloat16)
+    caches = {i: big[i] for i in range(layers)}
+    base, n, stride = _cache_geometry(caches)
+    assert base.data_ptr() == big.data_ptr() and n == layers
+    assert stride == B * cap * 2 * hk * d * 2
+    assert head_slice_bytes(caches, [5, 9], 2) == [2 * layers * 5 * 2 * d * 2,
+                                                   2 * layers * 9 * 2 * d * 2]
+    with pytest.raises(ValueError):  # layers out of order: not one strided region
+        _cache_geometry({0: big[0], 1: big[2], 2: big[1]})
+    with pytest.raises(ValueError):
+        _cache_geometry({i: big[i].transpose(-1, -2) for i in range(layers)})
