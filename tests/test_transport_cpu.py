@@ -180,8 +180,7 @@ def test_interop_with_reference_transport(tmp_path):
 def test_cache_geometry_and_head_slice_bytes():
     """The re-shard path's host checks: an engine cache is one all-layer tensor handed out as
     per-layer views at a fixed stride, and a head slice's packed size is K + V slabs of every
-    layer; views not at one fixed stride and rows
-    that are not contiguous are rejected."""
+    layer; views not at one fixed stride and rows that are not contiguous are rejected."""
     from hexgen2_b200.transport import _cache_geometry, head_slice_bytes
     layers, B, cap, hk, d = 3, 2, 16, 4, 8
     big = torch.zeros(layers, B, cap, 2, hk, d, dtype=torch.bfloat16)
