@@ -11,9 +11,7 @@ into hexgen2_b200.gpt.GPTLMHeadModel with strict=True and vice versa.
 from __future__ import annotations
 
 import hashlib
-import json
 import math
-import re
 import zlib
 from collections import OrderedDict
 from pathlib import Path

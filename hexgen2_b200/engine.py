@@ -18,8 +18,6 @@ reference's validation engine (transformers' eager LlamaForCausalLM, prefill / d
 """
 from __future__ import annotations
 
-from pathlib import Path
-
 import torch
 
 from . import ops

@@ -24,7 +24,7 @@ import torch.distributed as dist
 from torch import nn
 
 from . import ops
-from ._lib import HX_EPI_NONE, HX_EPI_RESIDUAL, HX_EPI_SWIGLU
+from ._lib import HX_EPI_RESIDUAL, HX_EPI_SWIGLU
 
 CausalLMOutput = namedtuple("CausalLMOutput", ["logits"])
 

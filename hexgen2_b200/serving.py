@@ -41,7 +41,6 @@ import torch.distributed as dist
 
 from . import ops
 from .engine import PREFILL_PROMPTS, PREFILL_TOKENS, ContinuousBatcher
-from .gpt import CacheState
 from .transport import KVHandoff
 
 ALIGN = 256  # ring offsets: 16 B suffices for the copy kernels; 256 keeps regions apart

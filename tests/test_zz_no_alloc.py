@@ -10,7 +10,6 @@ The cases cover both partial layouts that land in the static array: the balanced
 This file is named so pytest collects it last; it passes alone in a fresh process and after
 the rest of the suite.
 """
-import ctypes
 
 import pytest
 import torch
