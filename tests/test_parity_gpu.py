@@ -309,7 +309,7 @@ def test_packed_prefill_matches_reference_golden(hx, golden, fixture_dir, dtype)
     assert hx.ops.device_error() == 0
 
 
-def test_packed_prefill_equals_single_prompt_forward_7b_width(hx):
+def test_packed_prefill_as_close_to_truth_as_single_prompt_7b_width(hx):
     """Llama-2-7B widths (2 layers, bf16): ragged prompts in one packed pass against each
     prompt's own single-prompt forward and the f32 truth of the reference's algorithm. The two
     bf16 paths tile their projection GEMMs differently (M = one prompt vs the sum), so their
