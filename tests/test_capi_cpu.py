@@ -62,6 +62,12 @@ def test_ops_refuse_cpu_tensors():
         ops.gemm(torch.zeros(2, 8), torch.zeros(4, 8))
     with pytest.raises(ValueError, match="CUDA"):
         ops.rmsnorm(torch.zeros(2, 8), torch.ones(8), 1e-6)
+    q, cache = torch.zeros(3, 2, 8), torch.zeros(1, 4, 2, 1, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.prefill_attention_varlen(q, cache, [3], [0], 1, 0.5, torch.empty_like(q))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gemm_qkv_rotary_varlen(torch.zeros(3, 16), torch.zeros(32, 16), [3], [0], 2, 1, 8,
+                                   torch.zeros(4, 4), torch.zeros(4, 4), cache, q)
 
 
 def test_native_engine_refuses_cpu(tmp_path):
